@@ -1,0 +1,455 @@
+#!/usr/bin/env python
+"""Benchmark of the INT4 dequant-GEMV / GEMM path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (a "step"): one fused groupwise-INT4 dequant + matmul,
+y[1,4096] = x[1,4096] . W^T, W 4096x4096 INT4 with group 128 and fp32
+scales, fp16 activations ~ N(0,1), weights ~ N(0,0.02) -- the single-GPU
+decode GEMV.  Each step reads a different one of 64 weight copies (572 MB,
+4.5x the 126 MB L2), so every step streams its weights from HBM.  The K
+steps run as CUDA-graph replays of back-to-back launches on one stream and
+are timed with CUDA events; `value` is algorithmic bytes (8,937,472 per
+step) / time, summed over ranks.  Under torchrun each rank streams its own
+weight copies (weak scaling, no collective on the data path).
+
+`e2e` times the same step through the public API (openquant.triton_int4.
+int4_linear) with the activations copied from pinned host memory and the
+output read back to the host every step.
+
+`--impl reference` times the reference algorithm on the host cores (the
+oracle's NumPy restatement of dequantize_int4_groupwise + fp16 rounding +
+matmul, threaded over row blocks), each step a bounded row sample.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "INT4 dequant-GEMM: GB/s at M=1, TFLOP/s at M=2048, % of B200 roofline"
+UNIT = "GB/s"
+M, K, N, G = 1, 4096, 4096, 128
+KP = ((K + G - 1) // G) * G
+ALG_BYTES = N * KP // 2 + N * (KP // G) * 4 + M * K * 2 + M * N * 4  # 8,937,472
+COPIES = 64
+L2_BYTES = 126 * 1024 * 1024
+WORKLOAD = "int4_gemv_m1_k4096_n4096_g128_fp16"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def read_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return {k: float(p[k]) for k in FALLBACK_PEAKS}, "measured"
+    except (OSError, ValueError, KeyError):
+        return dict(FALLBACK_PEAKS), "fallback"
+
+
+def read_traffic(name):
+    """Per-launch DRAM bytes of the dominant kernel from a committed ncu
+    summary (profiles/<name>.json), or None."""
+    path = os.path.join(ROOT, "profiles", name + ".json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["dram_bytes_per_launch"])
+    except (OSError, ValueError, KeyError):
+        return None
+
+
+# ------------------------------------------------------------ clocks --
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples taken during the timed
+    region (read-only queries)."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+    def __init__(self, uuid):
+        self.uuid = uuid
+        self.proc = None
+        self.file = None
+
+    def start(self):
+        try:
+            self.file = tempfile.TemporaryFile(mode="w+")
+            cmd = ["nvidia-smi", "--query-gpu=" + self.FIELDS, "--format=csv,noheader,nounits", "-lms", "20"]
+            if self.uuid:
+                cmd += ["-i", self.uuid]
+            self.proc = subprocess.Popen(cmd, stdout=self.file, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        time.sleep(0.1)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.file.seek(0)
+        rows = [r.split(",") for r in self.file.read().strip().splitlines() if r.count(",") >= 8]
+        sm, smax, reasons = [], [], set()
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                smax.append(float(r[2]))
+            except ValueError:
+                continue
+            for name, val in zip(self.NAMES, r[5:9]):
+                if "Active" in val and "Not" not in val:
+                    reasons.add(name)
+        loaded = [s for s in sm if s > 0.5 * max(sm)] if sm else []
+        return {
+            "sm_mhz": statistics.median(loaded) if loaded else None,
+            "sm_max_mhz": max(smax) if smax else None,
+            "reasons": sorted(reasons),
+            "samples": len(sm),
+        }
+
+
+# ---------------------------------------------------------- CPU side --
+
+
+_CPU_LAYER = {}
+
+
+def _cpu_layer():
+    """The host copy of one INT4 layer (quantized once by the oracle)."""
+    if not _CPU_LAYER:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oq_oracle as orc
+
+        rng = np.random.default_rng(7)
+        w = rng.normal(0, 0.02, (N, K)).astype(np.float32)
+        data, scales = orc.quantize_int4_groupwise(w, G)
+        x = orc.round_to_dtype(rng.normal(size=(M, K)).astype(np.float32), "f16")
+        _CPU_LAYER.update(orc=orc, data=data.reshape(N, KP // 2), scales=scales, x=x)
+    return _CPU_LAYER
+
+
+def cpu_gemv_sample(rows, threads):
+    """One reference-algorithm step on the host: dequantize `rows` rows of
+    the INT4 layer, round them to fp16, multiply with x (fp32 BLAS).
+    Returns (seconds, algorithmic bytes of the sample)."""
+    layer = _cpu_layer()
+    orc, data2, scales, x = layer["orc"], layer["data"], layer["scales"], layer["x"]
+
+    def block(r0, r1):
+        wd = orc.dequantize_int4_groupwise(data2[r0:r1].reshape(-1), scales[r0:r1], (r1 - r0, K), G)
+        return x @ orc.round_to_dtype(wd, "f16").T
+
+    t0 = time.perf_counter()
+    y = np.concatenate(orc.threaded_rows(block, rows, threads=threads, min_rows=16), axis=1)
+    dt = time.perf_counter() - t0
+    assert y.shape == (M, rows)
+    sample_bytes = rows * KP // 2 + rows * (KP // G) * 4 + M * K * 2 + M * rows * 4
+    return dt, sample_bytes
+
+
+def cpu_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def cpu_baseline(budget_s=10.0):
+    threads = cpu_threads()
+    cpu_gemv_sample(N, threads)  # warm-up
+    times, nbytes = [], 0
+    t_end = time.perf_counter() + budget_s
+    while time.perf_counter() < t_end and len(times) < 50:
+        dt, nbytes = cpu_gemv_sample(N, threads)
+        times.append(dt)
+    med = statistics.median(times)
+    return {
+        "value": nbytes / med / 1e9,
+        "unit": UNIT,
+        "cores": threads,
+        "kind": "port",
+        "sample": f"{len(times)} full {N}x{K} g={G} layers (dequantize + fp16 round + x@W^T, NumPy/OpenBLAS, "
+                  f"{threads} threads), median {med * 1e3:.1f} ms",
+    }
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    threads = cpu_threads()
+    total = args.steps + args.warmup
+    budget = 120.0  # seconds for the whole run
+    dt_full, _ = cpu_gemv_sample(N, threads)
+    per_step = budget / max(total, 1)
+    rows = int(max(16, min(N, N * per_step / max(dt_full, 1e-6))))
+    for _ in range(args.warmup):
+        cpu_gemv_sample(rows, threads)
+    secs, nbytes = 0.0, 0
+    for _ in range(args.steps):
+        dt, b = cpu_gemv_sample(rows, threads)
+        secs += dt
+        nbytes += b
+    value = nbytes / secs / 1e9
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": value,
+        "unit": UNIT,
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": secs / args.steps * 1e3,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f16",
+        "data": "synthetic",
+        "config": {"workload": WORKLOAD, "sample_rows_per_step": rows, "l2": "host run"},
+        "cpu_baseline": {
+            "value": value,
+            "unit": UNIT,
+            "cores": threads,
+            "kind": "port",
+            "sample": f"{rows} of {N} rows of the layer per step (NumPy restatement of the reference's "
+                      f"dequantize_int4_groupwise + fp16 rounding + matmul, {threads} threads)",
+        },
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------- GPU side --
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    from openquant_b200 import _native as nat
+    from openquant_b200 import build
+    from openquant_b200.groupwise import quantize_int4_groupwise
+    from openquant.triton_int4 import int4_linear
+
+    build.build()
+    lib = nat.load()
+    nat.require_device()
+
+    gen = torch.Generator(device=dev).manual_seed(1000 + rank)
+    packs, scs, ys = [], [], []
+    for _ in range(COPIES):
+        w = torch.randn(N, K, generator=gen, device=dev).mul_(0.02).half()
+        q = quantize_int4_groupwise(w, G)
+        packs.append(q.data)
+        scs.append(q.scales)
+        ys.append(torch.empty(M, N, device=dev))
+        del w
+    x = torch.randn(M, K, generator=gen, device=dev).half()
+    torch.cuda.synchronize()
+
+    stream = torch.cuda.Stream(device=dev)
+    import ctypes
+
+    args_c = [
+        (ctypes.c_void_p(x.data_ptr()), nat.OQ_F16, ctypes.c_void_p(packs[i].data_ptr()),
+         ctypes.c_void_p(scs[i].data_ptr()), ctypes.c_void_p(ys[i].data_ptr()), M, N, K, G, 0, 0)
+        for i in range(COPIES)
+    ]
+
+    def launch_many(count, h):
+        for i in range(count):
+            st = lib.oq_int4_linear(*args_c[i % COPIES], h)
+            if st != 0:
+                raise RuntimeError(nat.last_error())
+
+    chunk = min(1024, max(1, args.steps))
+
+    def make_graph(count):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            launch_many(min(count, 8), ctypes.c_void_p(stream.cuda_stream))  # eager warm-up
+        stream.synchronize()
+        with torch.cuda.graph(g, stream=stream):
+            launch_many(count, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        return g
+
+    g_chunk = make_graph(chunk)
+    g_rest = make_graph(args.steps % chunk) if args.steps % chunk else None
+
+    # warm-up
+    wr = max(1, -(-args.warmup // chunk))
+    for _ in range(wr):
+        g_chunk.replay()
+    torch.cuda.synchronize()
+
+    uuid = None
+    try:
+        uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:
+        pass
+    clocks = ClockSampler(uuid)
+    clocks.start()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        for _ in range(args.steps // chunk):
+            g_chunk.replay()
+        if g_rest is not None:
+            g_rest.replay()
+        end.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    ms = start.elapsed_time(end)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+
+    # correctness spot check of the benchmarked kernel against torch.
+    from openquant_b200.groupwise import Groupwise4, dequantize_int4_groupwise
+
+    wref = dequantize_int4_groupwise(Groupwise4(packs[0], scs[0], (N, K), G)).half().double()
+    yref = x.double() @ wref.T
+    y0 = int4_linear(x, packs[0], scs[0], N, G)
+    rel = ((y0.double() - yref).norm() / yref.norm()).item()
+    assert rel < 1e-3, rel
+
+    # e2e through the public API with host buffers.
+    e2e_steps = min(args.steps, 2000)
+    x_host = x.cpu().pin_memory()
+    y_host = torch.empty(M, N).pin_memory()
+    x_dev = torch.empty_like(x)
+    for i in range(min(50, e2e_steps)):
+        x_dev.copy_(x_host, non_blocking=True)
+        int4_linear(x_dev, packs[i % COPIES], scs[i % COPIES], N, G, out=ys[i % COPIES])
+        y_host.copy_(ys[i % COPIES], non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for i in range(e2e_steps):
+        x_dev.copy_(x_host, non_blocking=True)
+        int4_linear(x_dev, packs[i % COPIES], scs[i % COPIES], N, G, out=ys[i % COPIES])
+        y_host.copy_(ys[i % COPIES], non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+    e2e_s = time.perf_counter() - t0
+    if world > 1:
+        t = torch.tensor([e2e_s], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+
+    peaks, src = read_peaks()
+    step_s = ms / 1e3 / args.steps
+    achieved = ALG_BYTES / step_s / 1e9
+    value = world * args.steps * ALG_BYTES / (ms / 1e3) / 1e9
+    traffic = read_traffic("gemv_m1_k4096_n4096_g128")
+    line = {
+        "metric": METRIC,
+        "value": value,
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": wr * chunk,
+        "ms_per_step": ms / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f16",
+        "data": "synthetic",
+        "config": {
+            "workload": WORKLOAD,
+            "m": M, "k": K, "n": N, "group_size": G,
+            "weights": f"{COPIES} distinct INT4 copies rotated ({COPIES * ALG_BYTES / 1e6:.0f} MB > L2)",
+            "l2": "inputs larger than L2 (weight-copy rotation), no flush",
+            "launch": "CUDA graph of back-to-back launches",
+            "parallelism": f"dp{world} (each rank streams its own weight copies)",
+        },
+        "roofline": {
+            "bound": "hbm",
+            "achieved": achieved,
+            "peak": peaks["hbm_gbs"],
+            "unit": "GB/s",
+            "frac": achieved / peaks["hbm_gbs"],
+            "traffic": traffic,
+            "peak_source": src,
+            "algorithmic_bytes_per_launch": ALG_BYTES,
+        },
+        "e2e": {
+            "value": world * e2e_steps * ALG_BYTES / e2e_s / 1e9,
+            "unit": UNIT,
+            "h2d_bytes_per_step": M * K * 2,
+            "d2h_bytes_per_step": M * N * 4,
+            "steps": e2e_steps,
+            "how": "int4_linear() per step: pinned H2D of x, kernel, D2H of y, stream sync",
+        },
+        "gpu_launches": args.steps,
+        "clocks": clk,
+        "check_rel_l2": rel,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline()
+    del g_chunk, g_rest
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200000)
+    ap.add_argument("--warmup", type=int, default=20000)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args(argv)
+    if args.steps < 1 or args.warmup < 0:
+        ap.error("steps must be >= 1 and warmup >= 0")
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,168 @@
+/*
+ * openquant_b200 C ABI.
+ *
+ * One shared library (openquant_b200/_lib/libopenquant_b200.so) exports the
+ * INT8 / INT4 quantize, dequantize and fused INT4 dequant-matmul entry points
+ * of the OpenQuant quantize-and-multiply path, as hand-written sm_100a CUDA
+ * kernels.  Every entry point:
+ *
+ *   - borrows caller-owned DEVICE pointers (inputs are never written);
+ *   - enqueues its kernels on the caller's CUDA stream (`stream`, a
+ *     cudaStream_t passed as void*; NULL = the legacy default stream) and
+ *     returns without synchronising;
+ *   - allocates no device memory;
+ *   - returns OQ_OK (0) or an error code; oq_last_error() then returns a
+ *     thread-local, NUL-terminated message.
+ *
+ * OQ_ERR_INVALID maps to Python's ValueError (bad shape, dtype, group size,
+ * alignment), OQ_ERR_CUDA / OQ_ERR_UNSUPPORTED to RuntimeError.
+ *
+ * Layouts are exactly the reference's (openquant 0.5.0):
+ *   per-row INT8   : q int8 [N*K] row-major, scales fp32 [N]
+ *   per-row INT4   : the row-major [N*K] int4 values flattened ACROSS row
+ *                    boundaries, two per byte (element 2i in the low nibble,
+ *                    2i+1 in the high nibble), odd totals padded with a zero
+ *                    nibble: ceil(N*K/2) bytes; scales fp32 [N]
+ *   groupwise INT4 : each row zero-padded to KP = ceil(K/g)*g columns and
+ *                    packed as above: N*KP/2 bytes, row r at byte r*KP/2;
+ *                    scales fp32 [N][KP/g]
+ * Nibbles are two's complement (-7..7 written; -8 decodes as -8).
+ */
+#ifndef OPENQUANT_B200_H
+#define OPENQUANT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void *oq_stream_t; /* a cudaStream_t */
+
+#if defined(__GNUC__)
+#define OQ_API __attribute__((visibility("default")))
+#else
+#define OQ_API
+#endif
+
+/* Status codes. */
+#define OQ_OK 0
+#define OQ_ERR_INVALID 1     /* argument error  -> ValueError   */
+#define OQ_ERR_CUDA 2        /* CUDA error       -> RuntimeError */
+#define OQ_ERR_UNSUPPORTED 3 /* no sm_100 device -> RuntimeError */
+
+/* Element types of weight / activation inputs. */
+#define OQ_F32 0
+#define OQ_F16 1
+#define OQ_BF16 2
+#define OQ_F64 3
+
+/* Fused-matmul kernel selection (oq_int4_linear `kernel` argument). */
+#define OQ_KERNEL_AUTO 0    /* choose from shape and the tile table       */
+#define OQ_KERNEL_GEMV 1    /* tensor-core GEMV, M <= 64, g % 32 == 0     */
+#define OQ_KERNEL_SIMT 2    /* CUDA-core kernel, any shape                */
+#define OQ_KERNEL_TCGEN05 3 /* tcgen05/TMEM GEMM, M >= 1, see oq_int4_linear */
+
+/* Library version string ("openquant_b200 <x.y.z> sm_100a"). */
+OQ_API const char *oq_version(void);
+
+/* Message of the last failed call on this thread ("" if none). */
+OQ_API const char *oq_last_error(void);
+
+/* Number of visible CUDA devices with compute capability 10.x, or -1 when
+ * the CUDA runtime cannot be initialised.  Never fails otherwise. */
+OQ_API int oq_device_count(void);
+
+/*
+ * Per-row symmetric INT8 quantize.
+ * Replaces quantize(weights, bits=8), openquant/quantization.py:14-40,
+ * :54-59 of the reference: scale[r] = max_c |w[r,c]| / 127 (fp32, IEEE
+ * division), 1.0 for an all-zero row; q = clip(rint(w / scale), -127, 127)
+ * with round-half-to-even and IEEE division; NaN quotients give 0.
+ *   w      : N*K elements of type `dtype` (device)
+ *   q      : N*K int8 (device, out)
+ *   scales : N fp32 (device, out)
+ */
+OQ_API int oq_quant_int8_rowwise(const void *w, int dtype, int64_t n, int64_t k,
+                          int8_t *q, float *scales, oq_stream_t stream);
+
+/*
+ * Per-row symmetric INT4 quantize with flat nibble packing.
+ * Replaces quantize(weights, bits=4), openquant/quantization.py:14-37,
+ * :41-52: scale[r] = max|w[r,:]| / 7; the int4 values of the whole
+ * row-major matrix are packed two per byte across row boundaries.
+ *   packed : ceil(N*K/2) bytes (device, out)
+ *   scales : N fp32 (device, out)
+ */
+OQ_API int oq_quant_int4_rowwise(const void *w, int dtype, int64_t n, int64_t k,
+                          uint8_t *packed, float *scales, oq_stream_t stream);
+
+/*
+ * Groupwise INT4 quantize.
+ * Replaces quantize_int4_groupwise(weights, group_size),
+ * openquant/groupwise.py:13-61: rows zero-padded to KP, scale = max|group| /
+ * 7.0 (1.0 for an all-zero group), q = clip(rint(w/scale), -7, 7), packed.
+ * group_size must be even and >= 2.
+ *   packed    : N*KP/2 bytes (device, out)
+ *   scales    : N*(KP/g) fp32 (device, out)
+ *   nonfinite : one int32 (device, out); set to 0, then to 1 if any input
+ *               element is NaN or +-Inf (the reference raises ValueError,
+ *               groupwise.py:22-23; the host wrapper does the same after
+ *               reading it).  May be NULL to skip the check.
+ */
+OQ_API int oq_quant_int4_group(const void *w, int dtype, int64_t n, int64_t k,
+                        int group_size, uint8_t *packed, float *scales,
+                        int32_t *nonfinite, oq_stream_t stream);
+
+/*
+ * Per-row INT8 dequantize: out[r,c] = (float)q[r,c] * scales[r].
+ * Replaces dequantize() for bits=8, openquant/quantization.py:62-64, :82,
+ * and decode_gpu(bits=8), openquant/gpu_benchmark.py:10-12, :30.
+ */
+OQ_API int oq_dequant_int8_rowwise(const int8_t *q, const float *scales, int64_t n,
+                            int64_t k, float *out, oq_stream_t stream);
+
+/*
+ * Per-row INT4 (flat-packed) dequantize: out[f] = int4(f) * scales[f / K]
+ * for f < N*K.  Replaces dequantize() for bits=4,
+ * openquant/quantization.py:65-78, :82, and decode_gpu(bits=4),
+ * openquant/gpu_benchmark.py:14-25, :30.
+ */
+OQ_API int oq_dequant_int4_rowwise(const uint8_t *packed, const float *scales,
+                            int64_t n, int64_t k, float *out,
+                            oq_stream_t stream);
+
+/*
+ * Groupwise INT4 dequantize to fp32 [N][K] (padding columns dropped).
+ * Replaces dequantize_int4_groupwise(q), openquant/groupwise.py:64-89, and
+ * restore_groupwise_torch(), openquant/group_benchmark.py:11-30.
+ */
+OQ_API int oq_dequant_int4_group(const uint8_t *packed, const float *scales,
+                          int64_t n, int64_t k, int group_size, float *out,
+                          oq_stream_t stream);
+
+/*
+ * Fused groupwise-INT4 dequant + matmul: y[M][N] (fp32) = x[M][K] . W^T where
+ * W[n][k] = round_to_x_dtype( (float)int4(n,k) * scales[n][k/g] ) -- the
+ * weight rounding of the reference kernel, openquant/triton_int4.py:62-65 --
+ * and products are accumulated in fp32.
+ * Replaces int4_linear(), openquant/triton_int4.py:78-138 (its Triton kernel
+ * _int4_matmul, :6-75).
+ *   x       : M*K fp16 or bf16, row-major, contiguous (device)
+ *   packed  : N*KP/2 bytes, the groupwise layout (device)
+ *   scales  : N*(KP/g) fp32 (device)
+ *   y       : M*N fp32 (device, out)
+ *   kernel  : OQ_KERNEL_* (AUTO picks by shape)
+ *   split_k : K-split count hint for the GEMV/SIMT kernels (0 = auto)
+ */
+OQ_API int oq_int4_linear(const void *x, int x_dtype, const uint8_t *packed,
+                   const float *scales, float *y, int64_t m, int64_t n,
+                   int64_t k, int group_size, int kernel, int split_k,
+                   oq_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* OPENQUANT_B200_H */

@@ -1,0 +1,3 @@
+"""openquant.gpu_benchmark -> openquant_b200.gpu_benchmark (reference module path)."""
+from openquant_b200.gpu_benchmark import *  # noqa: F401,F403
+from openquant_b200.gpu_benchmark import __all__  # noqa: F401

@@ -1,0 +1,84 @@
+"""int4_linear: fused groupwise-INT4 dequant + matmul on the B200.
+
+Drop-in for openquant/triton_int4.py:78-138.  The module keeps the
+reference's name so `from openquant.triton_int4 import int4_linear` keeps
+working, but it contains no Triton: the call goes through the C ABI
+(oq_int4_linear) to hand-written sm_100a kernels -- a tensor-core GEMV for
+the decode side (M <= 64), the tcgen05/TMEM GEMM for the prefill side, and a
+CUDA-core kernel for shapes neither covers.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _native as nat
+from . import tile_table
+
+__all__ = ["int4_linear"]
+
+
+def int4_linear(x, packed, scales, out_features, group_size, *, block_m=64, block_n=64, block_k=64, num_warps=4,
+                kernel=None, out=None):
+    """y = x @ W^T in fp32, W[n, k] = round_x(int4(n, k) * scales[n, k // g]).
+
+    Arguments and errors follow triton_int4.py:78-118 (ValueError for each
+    failed precondition), except that x may also be bf16.  The weight is
+    rounded to x's dtype after the fp32 multiply, as the reference kernel
+    does (triton_int4.py:62-65), and products accumulate in fp32.
+
+    block_m / block_n / block_k / num_warps are the reference's Triton tile
+    arguments; they are accepted (autotune-style callers pass them) and have
+    no effect on the result.  Kernel choice comes from the tuned tile table
+    (openquant_b200/tile_table.json) or `kernel` ("gemv", "simt",
+    "tcgen05"); `out` may supply a preallocated fp32 (M, N) tensor.
+    The launch is asynchronous on the current CUDA stream of x's device.
+    """
+    if x.ndim != 2 or x.dtype not in (torch.float16, torch.bfloat16):
+        raise ValueError("Input must be a 2D FP16 tensor")
+    if not x.is_cuda or not packed.is_cuda or not scales.is_cuda:
+        raise ValueError("All tensors must be on CUDA")
+    if not x.is_contiguous():
+        raise ValueError("Input must be contiguous")
+    if packed.dtype != torch.uint8:
+        raise ValueError("Packed weights must be uint8")
+    if scales.dtype != torch.float32:
+        raise ValueError("Scales must be float32")
+    if group_size < 2 or group_size % 2:
+        raise ValueError("Group size must be even and >= 2")
+    m, k = (int(v) for v in x.shape)
+    n = int(out_features)
+    g = int(group_size)
+    kp = ((k + g - 1) // g) * g
+    groups = kp // g
+    if m < 1 or n < 1 or k < 1:
+        raise ValueError("Matrix dimensions must be positive")
+    if tuple(scales.shape) != (n, groups):
+        raise ValueError("Incorrect scales shape")
+    if packed.numel() != n * kp // 2:
+        raise ValueError("Incorrect packed weight count")
+    if not packed.is_contiguous() or not scales.is_contiguous():
+        raise ValueError("Weights and scales must be contiguous")
+    if packed.device != x.device or scales.device != x.device:
+        raise ValueError("All tensors must use the same GPU")
+    for v in (block_m, block_n, block_k, num_warps):
+        if int(v) < 1:
+            raise ValueError("Tile arguments must be positive")
+
+    if out is None:
+        out = torch.empty((m, n), device=x.device, dtype=torch.float32)
+    elif (out.shape != (m, n) or out.dtype != torch.float32 or out.device != x.device
+          or not out.is_contiguous()):
+        raise ValueError("out must be a contiguous float32 (M, N) tensor on x's device")
+
+    nat.require_device()
+    if kernel is None:
+        sel, split = tile_table.lookup(m, n, k, g)
+    else:
+        if kernel not in nat.KERNELS:
+            raise ValueError(f"unknown kernel {kernel!r}")
+        sel, split = nat.KERNELS[kernel], 0
+    code = nat.OQ_F16 if x.dtype == torch.float16 else nat.OQ_BF16
+    with torch.cuda.device(x.device):
+        nat.check(nat.load().oq_int4_linear(nat.ptr(x), code, nat.ptr(packed), nat.ptr(scales), nat.ptr(out),
+                                            m, n, k, g, sel, split, nat.stream_of(x.device)))
+    return out

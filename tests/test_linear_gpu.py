@@ -1,0 +1,150 @@
+"""int4_linear vs the oracle's dequantise-then-matmul.
+
+The oracle rounds the dequantized weights to x's dtype before the product,
+as the reference kernel and its test do (triton_int4.py:62-65,
+tests/test_triton_int4.py:45-51), and sums in fp64.  Tolerances: rel-L2
+<= 1e-3 and max-abs <= 2e-2 (the bar for this path), and the reference
+test's own assert_close(rtol=0.02, atol=0.02).
+"""
+import numpy as np
+import pytest
+import torch
+
+import oq_oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+REL_L2 = 1e-3
+MAX_ABS = 2e-2
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _device():
+    if not torch.cuda.is_available():
+        pytest.skip("CUDA GPU required")
+    from openquant_b200 import build
+
+    build.build()
+
+
+def make_case(m, n, k, g, dtype, seed=42, w_sigma=1.0):
+    from openquant.groupwise import quantize_int4_groupwise
+
+    rng = np.random.default_rng(seed)
+    w = rng.normal(0, w_sigma, (n, k)).astype(np.float32)
+    x = rng.normal(size=(m, k)).astype(np.float32)
+    q = quantize_int4_groupwise(w, g)
+    xt = torch.from_numpy(x).cuda().to(dtype)
+    return x, q, xt
+
+
+def check_against_oracle(y, x, q, g, dtype):
+    name = "f16" if dtype == torch.float16 else "bf16"
+    ref = orc.int4_linear(x, q.data, q.scales, q.shape[0], g, x_dtype=name)
+    got = y.cpu().numpy()
+    assert got.shape == ref.shape and np.isfinite(got).all()
+    err = got.astype(np.float64) - ref
+    rel = np.linalg.norm(err) / max(np.linalg.norm(ref), 1e-30)
+    assert rel <= REL_L2, rel
+    assert np.abs(err).max() <= MAX_ABS, np.abs(err).max()
+    torch.testing.assert_close(torch.from_numpy(got), torch.from_numpy(ref), rtol=0.02, atol=0.02)
+    return rel
+
+
+@pytest.mark.parametrize("shape", [(3, 7, 65, 16), (16, 32, 128, 32), (33, 55, 79, 16)])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_reference_test_shapes(shape, dtype):
+    from openquant.triton_int4 import int4_linear
+
+    m, n, k, g = shape
+    x, q, xt = make_case(m, n, k, g, dtype)
+    y = int4_linear(xt, torch.from_numpy(q.data).cuda(), torch.from_numpy(q.scales).cuda(), n, g)
+    assert y.dtype == torch.float32 and y.shape == (m, n)
+    check_against_oracle(y, x, q, g, dtype)
+
+
+GEMV_SHAPES = [
+    (1, 16, 32, 32), (1, 17, 64, 32), (2, 48, 96, 32), (4, 100, 200, 64), (8, 33, 256, 128), (9, 64, 1024, 128),
+    (16, 4096, 4096, 128), (1, 4096, 4096, 128), (5, 31, 160, 32), (16, 8, 8, 32), (1, 1, 8, 32), (64, 70, 384, 128),
+    (40, 130, 520, 64), (1, 1000, 11008, 128),
+]
+
+
+@pytest.mark.parametrize("kernel", ["gemv", "simt", None])
+@pytest.mark.parametrize("shape", GEMV_SHAPES)
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_decode_kernels_vs_oracle(shape, dtype, kernel):
+    from openquant.triton_int4 import int4_linear
+
+    m, n, k, g = shape
+    if kernel == "simt" and m * n * k > 2e8:
+        pytest.skip("SIMT kernel checked on smaller shapes")
+    x, q, xt = make_case(m, n, k, g, dtype, seed=m * 7 + n + k, w_sigma=0.02)
+    y = int4_linear(xt, torch.from_numpy(q.data).cuda(), torch.from_numpy(q.scales).cuda(), n, g, kernel=kernel)
+    check_against_oracle(y, x, q, g, dtype)
+
+
+@pytest.mark.parametrize("shape", [(3, 20, 30, 2), (4, 9, 33, 6), (17, 40, 100, 10), (2, 16, 200, 16), (1, 5, 7, 8)])
+def test_simt_any_group_vs_oracle(shape):
+    from openquant.triton_int4 import int4_linear
+
+    m, n, k, g = shape
+    for dtype in (torch.float16, torch.bfloat16):
+        x, q, xt = make_case(m, n, k, g, dtype)
+        y = int4_linear(xt, torch.from_numpy(q.data).cuda(), torch.from_numpy(q.scales).cuda(), n, g)
+        check_against_oracle(y, x, q, g, dtype)
+
+
+def test_llama2_7b_decode_layer_set():
+    """M in {1, 4, 16} over the Llama-2-7B layer set, g = 128, fp16."""
+    from openquant.groupwise import quantize_int4_groupwise
+    from openquant.triton_int4 import int4_linear
+
+    for li, (k, n) in enumerate([(4096, 12288), (4096, 4096), (4096, 22016), (11008, 4096)]):
+        gen = torch.Generator(device="cuda").manual_seed(100 + li)
+        w = torch.randn(n, k, device="cuda", generator=gen).mul_(0.02).half()
+        q = quantize_int4_groupwise(w, 128)
+        wd = orc.dequantize_int4_groupwise(q.data.cpu().numpy(), q.scales.cpu().numpy(), (n, k), 128)
+        w16 = torch.from_numpy(orc.round_to_dtype(wd, "f16")).cuda().double()
+        for m in (1, 4, 16):
+            x = torch.randn(m, k, device="cuda", generator=gen).half()
+            y = int4_linear(x, q.data, q.scales, n, 128)
+            ref = x.double() @ w16.T
+            err = y.double() - ref
+            assert (err.norm() / ref.norm()).item() <= REL_L2
+            assert err.abs().max().item() <= MAX_ABS
+
+
+def test_out_argument_and_errors():
+    from openquant.triton_int4 import int4_linear
+
+    x, q, xt = make_case(4, 64, 128, 32, torch.float16)
+    p, s = torch.from_numpy(q.data).cuda(), torch.from_numpy(q.scales).cuda()
+    out = torch.full((4, 64), float("nan"), device="cuda")
+    y = int4_linear(xt, p, s, 64, 32, out=out)
+    assert y.data_ptr() == out.data_ptr()
+    check_against_oracle(y, x, q, 32, torch.float16)
+    with pytest.raises(ValueError, match="scales shape"):
+        int4_linear(xt, p, s[:, :1].contiguous(), 64, 32)
+    with pytest.raises(ValueError, match="packed weight count"):
+        int4_linear(xt, p[:-1], s, 64, 32)
+    with pytest.raises(ValueError, match="contiguous"):
+        int4_linear(xt.t().contiguous().t(), p, s, 64, 32)
+    with pytest.raises(ValueError, match="Group size"):
+        int4_linear(xt, p, s, 64, 3)
+    with pytest.raises(ValueError, match="uint8"):
+        int4_linear(xt, p.to(torch.int8), s, 64, 32)
+    with pytest.raises(ValueError, match="float32"):
+        int4_linear(xt, p, s.double(), 64, 32)
+    with pytest.raises(ValueError):
+        int4_linear(xt, p, s, 64, 32, kernel="gemv", out=torch.empty(3, 3, device="cuda"))
+
+
+def test_deterministic_repeat():
+    from openquant.triton_int4 import int4_linear
+
+    x, q, xt = make_case(16, 512, 4096, 128, torch.bfloat16)
+    p, s = torch.from_numpy(q.data).cuda(), torch.from_numpy(q.scales).cuda()
+    a = int4_linear(xt, p, s, 512, 128)
+    b = int4_linear(xt, p, s, 512, 128)
+    assert torch.equal(a, b)
