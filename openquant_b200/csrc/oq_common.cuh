@@ -138,9 +138,8 @@ __device__ __forceinline__ uint32_t quant_bits(float w, float s, float inv_s, fl
     float d = __fsub_rn(r, rr);
     if (!(fabsf(d) < 0.499f && fabsf(rr) <= qmax)) {
         float e = __fdiv_rn(w, s);
-        e = rintf(e);
-        e = fminf(fmaxf(e, -qmax), qmax);
-        if (e != e) e = 0.0f;  // NaN
+        // NaN first: fmaxf/fminf would turn a NaN into -qmax.
+        e = (e != e) ? 0.0f : fminf(fmaxf(rintf(e), -qmax), qmax);
         t = __fadd_rn(e, kRoundMagic);
     }
     return __float_as_uint(t);

@@ -58,25 +58,92 @@ __device__ __forceinline__ float dq(uint32_t word, int i, float s) {
     return __fmul_rn(__fsub_rn(f, 8388616.0f), s);                               // (u - 8) * s
 }
 
+// Per-(row, group) multipliers of dq_word: s * 16^-p for the nibble
+// positions p the word is split into, and -8s.
+struct DqScale {
+    float2 mul[4];
+    float2 m8s;
+    bool fast;  // s * 2^-16 is a normal float and 8s is finite
+};
+
+__device__ __forceinline__ DqScale make_dq_scale(float s) {
+    DqScale d;
+    const float s4 = s * 0.0625f, s8 = s * 0.00390625f, s12 = s * 0.000244140625f, s16 = s * 1.52587890625e-05f;
+    d.mul[0] = make_float2(s, s4);
+    d.mul[1] = make_float2(s8, s12);
+    d.mul[2] = make_float2(s16, s8);
+    d.mul[3] = make_float2(s12, s16);
+    d.m8s = make_float2(-8.0f * s, -8.0f * s);
+    const float a = fabsf(s);
+    d.fast = (a >= 0x1p-100f && a <= 0x1p100f);
+    return d;
+}
+
+// Eight weights of one packed word (raw two's-complement nibbles, element i
+// in bits 4i..4i+3) -> four packed pairs {w(2j), w(2j+1)} of
+// round_x(fl32(q * s)).  The nibbles are lifted into fp32 as 2^23 + u*16^p
+// (u = q + 8, offset binary, p = the nibble's position after at most one
+// 12-bit shift) by AND/XOR into the 0x4B000000 exponent; subtracting 2^23 is
+// exact, and fma(u*16^p, s*16^-p, -8s) is the exact value (u - 8) * s = q * s
+// rounded once -- the reference's fp32 product.  Blackwell's packed
+// f32x2 add/fma do two weights per instruction.  Scales whose 16^-4 multiple
+// would be subnormal (or non-finite) take the per-nibble path.
+template <typename XT>
+__device__ __forceinline__ void dq_word(uint32_t w, const DqScale &sc, float s, uint32_t (&h)[4]) {
+    if (sc.fast) {
+        const uint32_t wh = w >> 12;
+        const float f0 = __uint_as_float((w & 0x0000000Fu) ^ 0x4B000008u);
+        const float f1 = __uint_as_float((w & 0x000000F0u) ^ 0x4B000080u);
+        const float f2 = __uint_as_float((w & 0x00000F00u) ^ 0x4B000800u);
+        const float f3 = __uint_as_float((w & 0x0000F000u) ^ 0x4B008000u);
+        const float f4 = __uint_as_float((w & 0x000F0000u) ^ 0x4B080000u);
+        const float f5 = __uint_as_float((wh & 0x00000F00u) ^ 0x4B000800u);
+        const float f6 = __uint_as_float((wh & 0x0000F000u) ^ 0x4B008000u);
+        const float f7 = __uint_as_float((wh & 0x000F0000u) ^ 0x4B080000u);
+        const float2 m23 = make_float2(-8388608.0f, -8388608.0f);
+        const float2 w01 = __ffma2_rn(__fadd2_rn(make_float2(f0, f1), m23), sc.mul[0], sc.m8s);
+        const float2 w23 = __ffma2_rn(__fadd2_rn(make_float2(f2, f3), m23), sc.mul[1], sc.m8s);
+        const float2 w45 = __ffma2_rn(__fadd2_rn(make_float2(f4, f5), m23), sc.mul[2], sc.m8s);
+        const float2 w67 = __ffma2_rn(__fadd2_rn(make_float2(f6, f7), m23), sc.mul[3], sc.m8s);
+        h[0] = XTraits<XT>::pack(w01.x, w01.y);
+        h[1] = XTraits<XT>::pack(w23.x, w23.y);
+        h[2] = XTraits<XT>::pack(w45.x, w45.y);
+        h[3] = XTraits<XT>::pack(w67.x, w67.y);
+    } else {
+        const uint32_t u = w ^ 0x88888888u;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) h[j] = XTraits<XT>::pack(dq(u, 2 * j, s), dq(u, 2 * j + 1, s));
+    }
+}
+
 // ------------------------------------------------------------- GEMV ----
 //
-// One CTA = 16 weight rows x the whole K, split over WARPS warps (chunks of
-// 128 columns dealt round-robin, partial sums reduced through shared memory
-// in a fixed order, so results are deterministic).  In a warp, lane (g, t)
-// (g = lane/4, t = lane%4) loads 16 bytes = 32 columns of rows g and g+8 at
-// column 128*chunk + 32*t and feeds them to mma.m16n8k16 with the weight tile
-// as the A operand (16 rows x 16 "slots") and x^T as B (slots x 8 batch
-// columns).  The k-slots {2t, 2t+1, 2t+8, 2t+9} of a lane carry four
-// consecutive real columns of its own 32-column segment; the B fragment is
-// loaded with the same permutation, so the tensor-core sum over slots is the
-// sum over real columns.  NT n-tiles cover M <= 8*NT.
-template <typename XT, int NT, int WARPS>
+// One CTA = 16 weight rows x the whole K, split over WARPS warps: 128-column
+// chunks are dealt round-robin to the warps and their partial sums reduced
+// through shared memory in a fixed order (deterministic results).
+//
+// Memory-level parallelism: each warp keeps U chunks of packed weights in
+// flight in a register ring (a chunk = 2 rows x 16 bytes per lane), and the
+// first U loads are issued before griddepcontrol.wait, so under programmatic
+// dependent launch they overlap the previous kernel's tail (weights never
+// depend on it; x and y are touched only after the wait).
+//
+// Tensor cores: lane (g, t) (g = lane/4, t = lane%4) owns rows g and g+8 and
+// columns 128*chunk + 32*t .. +32 and feeds mma.m16n8k16 with the weight tile
+// as A (16 rows x 16 "slots") and x^T as B (slots x 8 batch columns).  The
+// k-slots {2t, 2t+1, 2t+8, 2t+9} of a lane carry four consecutive real
+// columns of its own segment, and B is loaded with the same permutation, so
+// the tensor-core sum over slots is the sum over real columns.  NT n-tiles
+// cover M <= 8*NT.  x is staged in shared memory when it fits (XS).
+template <typename XT, int NT, int WARPS, int U, bool XS>
 __global__ void __launch_bounds__(WARPS * 32) gemv_int4_kernel(const XT *__restrict__ x,
                                                                const uint8_t *__restrict__ packed,
                                                                const float *__restrict__ scales,
                                                                float *__restrict__ y, int m, int64_t n, int64_t k,
                                                                int64_t kp, int g) {
+    extern __shared__ uint4 xs_raw[];
     __shared__ float red[WARPS][NT][4][32];
+    const XT *xs = reinterpret_cast<const XT *>(xs_raw);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int gi = lane >> 2, t = lane & 3;
     const int64_t row0 = (int64_t)blockIdx.x * 16;
@@ -86,52 +153,84 @@ __global__ void __launch_bounds__(WARPS * 32) gemv_int4_kernel(const XT *__restr
     const int64_t nchunks = cdiv(kp, 128);
     const uint8_t *pa = packed + ra * (kp / 2);
     const uint8_t *pb = packed + rb * (kp / 2);
+    const float *sra = scales + ra * groups;
+    const float *srb = scales + rb * groups;
+
+    uint4 wa[U], wb[U];
+    float sa[U], sb[U];
+    auto load = [&](int u, int64_t c) {
+        const int64_t k0 = 128 * c + 32 * t;
+        wa[u] = make_uint4(0, 0, 0, 0);
+        wb[u] = make_uint4(0, 0, 0, 0);
+        sa[u] = 0.0f;
+        sb[u] = 0.0f;
+        if (c < nchunks && k0 < kp) {
+            if (va) {
+                wa[u] = __ldg(reinterpret_cast<const uint4 *>(pa + k0 / 2));
+                sa[u] = __ldg(sra + k0 / g);
+            }
+            if (vb) {
+                wb[u] = __ldg(reinterpret_cast<const uint4 *>(pb + k0 / 2));
+                sb[u] = __ldg(srb + k0 / g);
+            }
+        }
+    };
+#pragma unroll
+    for (int u = 0; u < U; ++u) load(u, warp + (int64_t)u * WARPS);
+
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;");
+
+    if (XS) {  // stage x [m][k] (k % 8 == 0) in shared memory
+        const int64_t vecs = (int64_t)m * k / 8;
+        for (int64_t i = threadIdx.x; i < vecs; i += blockDim.x)
+            xs_raw[i] = __ldg(reinterpret_cast<const uint4 *>(x) + i);
+        __syncthreads();
+    }
 
     float acc[NT][4];
 #pragma unroll
     for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
 
-    for (int64_t c = warp; c < nchunks; c += WARPS) {
-        const int64_t k0 = 128 * c + 32 * t;  // first column of this lane's segment
-        uint4 wa = make_uint4(0, 0, 0, 0), wb = make_uint4(0, 0, 0, 0);
-        float sa = 0.0f, sb = 0.0f;
-        if (k0 < kp) {
-            if (va) {
-                wa = __ldg(reinterpret_cast<const uint4 *>(pa + k0 / 2));
-                sa = __ldg(scales + ra * groups + k0 / g);
-            }
-            if (vb) {
-                wb = __ldg(reinterpret_cast<const uint4 *>(pb + k0 / 2));
-                sb = __ldg(scales + rb * groups + k0 / g);
-            }
-        }
-        const uint32_t wa4[4] = {wa.x ^ 0x88888888u, wa.y ^ 0x88888888u, wa.z ^ 0x88888888u, wa.w ^ 0x88888888u};
-        const uint32_t wb4[4] = {wb.x ^ 0x88888888u, wb.y ^ 0x88888888u, wb.z ^ 0x88888888u, wb.w ^ 0x88888888u};
+    const int64_t mine = nchunks > warp ? cdiv(nchunks - warp, WARPS) : 0;  // chunks of this warp
+    for (int64_t base = 0; base < mine; base += U) {
 #pragma unroll
-        for (int wd = 0; wd < 4; ++wd) {
-            const int64_t kw = k0 + 8 * wd;  // columns kw..kw+7
-            // B fragments: x[batch][kw..kw+7] for batch = 8*j + gi.
-            uint4 xb[NT];
+        for (int u = 0; u < U; ++u) {
+            const int64_t c = warp + (base + u) * WARPS;
+            if (base + u < mine) {
+                const int k0 = (int)(128 * c + 32 * t);
+                const uint32_t qa[4] = {wa[u].x, wa[u].y, wa[u].z, wa[u].w};
+                const uint32_t qb[4] = {wb[u].x, wb[u].y, wb[u].z, wb[u].w};
+                const DqScale dsa = make_dq_scale(sa[u]), dsb = make_dq_scale(sb[u]);
 #pragma unroll
-            for (int j = 0; j < NT; ++j) {
-                const int mb = 8 * j + gi;
-                xb[j] = (mb < m && kw < k) ? __ldg(reinterpret_cast<const uint4 *>(x + (int64_t)mb * k + kw))
-                                           : make_uint4(0, 0, 0, 0);
-            }
-            // Two k16 steps per word: nibbles 0-3, then 4-7.
+                for (int wd = 0; wd < 4; ++wd) {
+                    const int kw = k0 + 8 * wd;  // columns kw..kw+7
+                    uint4 xb[NT];
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const uint32_t a0 = XTraits<XT>::pack(dq(wa4[wd], 4 * h, sa), dq(wa4[wd], 4 * h + 1, sa));
-                const uint32_t a2 = XTraits<XT>::pack(dq(wa4[wd], 4 * h + 2, sa), dq(wa4[wd], 4 * h + 3, sa));
-                const uint32_t a1 = XTraits<XT>::pack(dq(wb4[wd], 4 * h, sb), dq(wb4[wd], 4 * h + 1, sb));
-                const uint32_t a3 = XTraits<XT>::pack(dq(wb4[wd], 4 * h + 2, sb), dq(wb4[wd], 4 * h + 3, sb));
+                    for (int j = 0; j < NT; ++j) {
+                        const int mb = 8 * j + gi;
+                        if (mb < m && kw < k)
+                            xb[j] = XS ? *reinterpret_cast<const uint4 *>(xs + mb * (int)k + kw)
+                                       : __ldg(reinterpret_cast<const uint4 *>(x + (int64_t)mb * k + kw));
+                        else
+                            xb[j] = make_uint4(0, 0, 0, 0);
+                    }
+                    uint32_t ha[4], hb[4];
+                    dq_word<XT>(qa[wd], dsa, sa[u], ha);
+                    dq_word<XT>(qb[wd], dsb, sb[u], hb);
+                    // k16 step 0: nibbles 0-3 (pairs 0, 1); step 1: nibbles 4-7.
 #pragma unroll
-                for (int j = 0; j < NT; ++j) {
-                    const uint32_t b0 = h == 0 ? xb[j].x : xb[j].z;
-                    const uint32_t b1 = h == 0 ? xb[j].y : xb[j].w;
-                    XTraits<XT>::mma(acc[j], a0, a1, a2, a3, b0, b1);
+                    for (int h = 0; h < 2; ++h) {
+#pragma unroll
+                        for (int j = 0; j < NT; ++j) {
+                            const uint32_t b0 = h == 0 ? xb[j].x : xb[j].z;
+                            const uint32_t b1 = h == 0 ? xb[j].y : xb[j].w;
+                            XTraits<XT>::mma(acc[j], ha[2 * h], hb[2 * h], ha[2 * h + 1], hb[2 * h + 1], b0, b1);
+                        }
+                    }
                 }
             }
+            load(u, warp + (base + u + U) * WARPS);  // refill the slot
         }
     }
 
@@ -186,18 +285,52 @@ __global__ void __launch_bounds__(256) simt_int4_kernel(const XT *__restrict__ x
     }
 }
 
+// Launch with programmatic stream serialization: a GEMV that follows
+// another kernel in the stream may start (and prefetch its weights) while
+// that kernel drains.  Without a preceding PDL-aware kernel it behaves like a
+// normal launch.
+template <typename Kern, typename XT>
+int launch_pdl(Kern kern, unsigned blocks, unsigned threads, size_t smem, cudaStream_t st, const XT *x,
+               const uint8_t *packed, const float *scales, float *y, int m, int64_t n, int64_t k, int64_t kp, int g) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(blocks);
+    cfg.blockDim = dim3(threads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t err = cudaLaunchKernelEx(&cfg, kern, x, packed, scales, y, m, n, k, kp, g);
+    if (err != cudaSuccess) {
+        set_error("int4_linear (GEMV): launch failed: %s", cudaGetErrorString(err));
+        return OQ_ERR_CUDA;
+    }
+    return OQ_OK;
+}
+
+template <typename XT, int NT, int WARPS, int U>
+int launch_gemv_t(const XT *x, const uint8_t *packed, const float *scales, float *y, int64_t m, int64_t n,
+                  int64_t k, int64_t kp, int g, cudaStream_t st) {
+    const unsigned blocks = (unsigned)cdiv(n, 16);
+    const size_t xbytes = (size_t)m * (size_t)k * sizeof(XT);
+    if (xbytes <= 48 * 1024 - sizeof(float) * WARPS * NT * 128)
+        return launch_pdl(gemv_int4_kernel<XT, NT, WARPS, U, true>, blocks, WARPS * 32, xbytes, st, x, packed,
+                          scales, y, (int)m, n, k, kp, g);
+    return launch_pdl(gemv_int4_kernel<XT, NT, WARPS, U, false>, blocks, WARPS * 32, 0, st, x, packed, scales, y,
+                      (int)m, n, k, kp, g);
+}
+
 template <typename XT>
 int launch_gemv(const XT *x, const uint8_t *packed, const float *scales, float *y, int64_t m, int64_t n, int64_t k,
                 int64_t kp, int g, cudaStream_t st) {
-    constexpr int W = 8;
-    const unsigned blocks = (unsigned)cdiv(n, 16);
     switch ((m + 7) / 8) {
-        case 1: gemv_int4_kernel<XT, 1, W><<<blocks, W * 32, 0, st>>>(x, packed, scales, y, (int)m, n, k, kp, g); break;
-        case 2: gemv_int4_kernel<XT, 2, W><<<blocks, W * 32, 0, st>>>(x, packed, scales, y, (int)m, n, k, kp, g); break;
-        case 3: case 4: gemv_int4_kernel<XT, 4, W><<<blocks, W * 32, 0, st>>>(x, packed, scales, y, (int)m, n, k, kp, g); break;
-        default: gemv_int4_kernel<XT, 8, W><<<blocks, W * 32, 0, st>>>(x, packed, scales, y, (int)m, n, k, kp, g); break;
+        case 1: return launch_gemv_t<XT, 1, 8, 4>(x, packed, scales, y, m, n, k, kp, g, st);
+        case 2: return launch_gemv_t<XT, 2, 8, 4>(x, packed, scales, y, m, n, k, kp, g, st);
+        case 3: case 4: return launch_gemv_t<XT, 4, 8, 2>(x, packed, scales, y, m, n, k, kp, g, st);
+        default: return launch_gemv_t<XT, 8, 8, 2>(x, packed, scales, y, m, n, k, kp, g, st);
     }
-    return check_launch("int4_linear (GEMV)");
 }
 
 template <typename XT>

@@ -48,10 +48,21 @@ def assert_matches_golden(golden, key, actual, exact=True, atol=0.0):
     actual = actual.reshape(expected.shape)
     if exact:
         if expected.dtype.kind == "f":
-            np.testing.assert_array_equal(actual.view(np.uint32) if actual.dtype == np.float32 else actual,
-                                          expected.view(np.uint32) if expected.dtype == np.float32 else expected,
-                                          err_msg=key)
+            assert_float_bits_equal(actual, expected, key)
         else:
             np.testing.assert_array_equal(actual, expected, err_msg=key)
     else:
         np.testing.assert_allclose(actual, expected, rtol=0, atol=atol, err_msg=key)
+
+
+def assert_float_bits_equal(actual, expected, msg=""):
+    """Bit-for-bit equality of float arrays (so -0.0 != +0.0), except that a
+    NaN only has to meet a NaN: x86 and NVIDIA GPUs write different NaN
+    payloads (0x7FC00000 / 0xFFC00000 vs 0x7FFFFFFF), which carry no value."""
+    actual = np.asarray(actual, dtype=np.float32)
+    expected = np.asarray(expected, dtype=np.float32)
+    assert actual.shape == expected.shape, (msg, actual.shape, expected.shape)
+    nan_a, nan_e = np.isnan(actual), np.isnan(expected)
+    np.testing.assert_array_equal(nan_a, nan_e, err_msg=f"{msg}: NaN positions")
+    keep = ~nan_e
+    np.testing.assert_array_equal(actual.view(np.uint32)[keep], expected.view(np.uint32)[keep], err_msg=msg)

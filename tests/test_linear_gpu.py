@@ -148,3 +148,31 @@ def test_deterministic_repeat():
     a = int4_linear(xt, p, s, 512, 128)
     b = int4_linear(xt, p, s, 512, 128)
     assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("kernel", ["gemv", "simt", None])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("shape", [(48, 512, 128), (33, 256, 64), (40, 96, 32)])
+def test_weight_rounding_is_bit_exact(shape, dtype, kernel):
+    """One-hot activation rows: y[m, n] = x[m, k_m] * W[n, k_m] with x = 1, a
+    single exact product, so y must equal round_x(fl32(q * s)) bit for bit
+    (the weight rounding of triton_int4.py:62-65) for every column probed."""
+    from openquant.groupwise import quantize_int4_groupwise
+    from openquant.triton_int4 import int4_linear
+    from conftest import assert_float_bits_equal
+
+    n, k, g = shape
+    m = 64 if kernel != "simt" else 16
+    rng = np.random.default_rng(n + k + g)
+    w = rng.normal(0, 0.05, (n, k)).astype(np.float32)
+    w[:, ::7] *= 1e-3  # small groups exercise other exponents
+    q = quantize_int4_groupwise(w, g)
+    name = "f16" if dtype == torch.float16 else "bf16"
+    wref = orc.round_to_dtype(orc.dequantize_int4_groupwise(q.data, q.scales, (n, k), g), name)
+    p, s = torch.from_numpy(q.data).cuda(), torch.from_numpy(q.scales).cuda()
+    for start in range(0, k, m):
+        cols = np.arange(start, min(k, start + m))
+        x = np.zeros((len(cols), k), np.float32)
+        x[np.arange(len(cols)), cols] = 1.0
+        y = int4_linear(torch.from_numpy(x).cuda().to(dtype), p, s, n, g, kernel=kernel)
+        assert_float_bits_equal(y.cpu().numpy(), wref[:, cols].T.copy(), f"cols {start}")
