@@ -64,6 +64,14 @@ typedef void *oq_stream_t; /* a cudaStream_t */
 #define OQ_KERNEL_SIMT 2    /* CUDA-core kernel, any shape                */
 #define OQ_KERNEL_TCGEN05 3 /* tcgen05/TMEM GEMM, M >= 1, see oq_int4_linear */
 
+/* oq_int4_linear `config` flag: round every weight to x's dtype exactly as
+ * the reference kernel does (fp32 q*scale, then fp16/bf16).  Without it an
+ * fp16 GEMV with group_size % 128 == 0 multiplies x by the exact integer
+ * nibbles and applies each fp32 group scale to the group's fp32 partial
+ * sum -- closer to x.(q*s) than the reference, within the parity tolerance
+ * of it, and ~2.5x fewer instructions per weight. */
+#define OQ_CONFIG_EXACT_ROUNDING 16
+
 /* Library version string ("openquant_b200 <x.y.z> sm_100a"). */
 OQ_API const char *oq_version(void);
 
@@ -73,6 +81,15 @@ OQ_API const char *oq_last_error(void);
 /* Number of visible CUDA devices with compute capability 10.x, or -1 when
  * the CUDA runtime cannot be initialised.  Never fails otherwise. */
 OQ_API int oq_device_count(void);
+
+/*
+ * Synchronises the current device, then reads and clears the device-side
+ * error word of the library's pipelined kernels: *code = 0 when none, 1 when
+ * a kernel gave up waiting on one of its internal pipeline barriers (it then
+ * returned early, its outputs are undefined).  No reference counterpart:
+ * the reference's Triton kernel has no internal waits.
+ */
+OQ_API int oq_take_device_error(int32_t *code);
 
 /*
  * Per-row symmetric INT8 quantize.
@@ -154,11 +171,19 @@ OQ_API int oq_dequant_int4_group(const uint8_t *packed, const float *scales,
  *   scales  : N*(KP/g) fp32 (device)
  *   y       : M*N fp32 (device, out)
  *   kernel  : OQ_KERNEL_* (AUTO picks by shape)
- *   split_k : K-split count hint for the GEMV/SIMT kernels (0 = auto)
+ *   config  : low 4 bits: launch-shape index of the chosen kernel (0 =
+ *             default); for the GEMV, 1..7 select register-ring launch
+ *             shapes (warps per CTA, chunks in flight per warp, CTAs per
+ *             SM) = (8,4,2) (16,2,2) (12,2,2) (16,1,2) (8,2,3) (8,2,4)
+ *             (8,4,4), and 8, 9, 10 the TMA-fed kernel with 8 or 16
+ *             consumer warps and one CTA per SM, or 8 warps and two CTAs per
+ *             SM (M <= 16) -- only the fp32 summation order changes;
+ *             `openquant tune` picks it.  | OQ_CONFIG_EXACT_ROUNDING: see
+ *             above.
  */
 OQ_API int oq_int4_linear(const void *x, int x_dtype, const uint8_t *packed,
                    const float *scales, float *y, int64_t m, int64_t n,
-                   int64_t k, int group_size, int kernel, int split_k,
+                   int64_t k, int group_size, int kernel, int config,
                    oq_stream_t stream);
 
 #ifdef __cplusplus

@@ -17,6 +17,7 @@ from .build import LIB
 OQ_OK, OQ_ERR_INVALID, OQ_ERR_CUDA, OQ_ERR_UNSUPPORTED = 0, 1, 2, 3
 OQ_F32, OQ_F16, OQ_BF16, OQ_F64 = 0, 1, 2, 3
 KERNELS = {"auto": 0, "gemv": 1, "simt": 2, "tcgen05": 3}
+CONFIG_EXACT_ROUNDING = 16
 
 # name -> (restype, argtypes), exactly the declarations of the header.
 _P, _I64, _I32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
@@ -24,6 +25,7 @@ SIGNATURES = {
     "oq_version": (ctypes.c_char_p, []),
     "oq_last_error": (ctypes.c_char_p, []),
     "oq_device_count": (_I32, []),
+    "oq_take_device_error": (_I32, [_P]),
     "oq_quant_int8_rowwise": (_I32, [_P, _I32, _I64, _I64, _P, _P, _P]),
     "oq_quant_int4_rowwise": (_I32, [_P, _I32, _I64, _I64, _P, _P, _P]),
     "oq_quant_int4_group": (_I32, [_P, _I32, _I64, _I64, _I32, _P, _P, _P, _P]),

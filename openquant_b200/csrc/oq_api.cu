@@ -1,7 +1,8 @@
 // Error state, version and device queries of the openquant_b200 C ABI.
-#include "oq_common.cuh"
+#include "oq_sm100.cuh"
 
 #include <mutex>
+#include <vector>
 
 namespace oq {
 
@@ -55,7 +56,80 @@ int sm_count() {
     return cached[dev];
 }
 
+namespace {
+std::mutex g_reader_mu;
+std::vector<DeviceErrorReader> &readers() {
+    static std::vector<DeviceErrorReader> v;
+    return v;
+}
+}  // namespace
+
+void register_device_error_reader(DeviceErrorReader fn) {
+    std::lock_guard<std::mutex> lock(g_reader_mu);
+    readers().push_back(fn);
+}
+
+int make_tensor_map_2d(CUtensorMap *map, const void *base, CUtensorMapDataType dtype, int esize, uint64_t inner,
+                       uint64_t outer, uint64_t pitch_bytes, uint32_t box_inner, uint32_t box_outer,
+                       CUtensorMapSwizzle swizzle) {
+    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+    static std::mutex mu;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (encode == nullptr) {
+            cudaDriverEntryPointQueryResult q;
+            void *fn = nullptr;
+            cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+            if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || fn == nullptr) {
+                set_error("cuTensorMapEncodeTiled unavailable (driver too old?)");
+                return OQ_ERR_UNSUPPORTED;
+            }
+            encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+        }
+    }
+    if (!aligned(base, 16) || pitch_bytes % 16 != 0 || (uint64_t)box_inner * esize % 16 != 0) {
+        set_error("tensor map: base, pitch and box row must be 16-byte multiples");
+        return OQ_ERR_INVALID;
+    }
+    cuuint64_t dims[2] = {inner, outer};
+    cuuint64_t strides[1] = {pitch_bytes};
+    cuuint32_t box[2] = {box_inner, box_outer};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = encode(map, dtype, 2, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_error("cuTensorMapEncodeTiled failed (code %d)", (int)r);
+        return OQ_ERR_CUDA;
+    }
+    return OQ_OK;
+}
+
 }  // namespace oq
+
+extern "C" int oq_take_device_error(int32_t *code) {
+    oq::clear_error();
+    if (code == nullptr) return oq::invalid("null pointer argument");
+    *code = 0;
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        oq::set_error("cudaDeviceSynchronize failed: %s", cudaGetErrorString(e));
+        return OQ_ERR_CUDA;
+    }
+    std::vector<oq::DeviceErrorReader> rs;
+    {
+        std::lock_guard<std::mutex> lock(oq::g_reader_mu);
+        rs = oq::readers();
+    }
+    int c = 0;
+    for (auto fn : rs) {
+        if (fn(&c) != OQ_OK) {
+            oq::set_error("reading the device error word failed");
+            return OQ_ERR_CUDA;
+        }
+    }
+    *code = c;
+    return OQ_OK;
+}
 
 extern "C" const char *oq_version(void) { return "openquant_b200 0.1.0 sm_100a"; }
 

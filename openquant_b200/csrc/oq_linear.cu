@@ -6,7 +6,10 @@
 // activation type, as openquant/triton_int4.py:62-65 does -- and x * w is
 // accumulated in fp32.  fl32(q*s) is formed exactly: q = (2^23 + u) -
 // (2^23 + 8) with u the offset-binary nibble is exact, then one fp32 multiply.
-#include "oq_common.cuh"
+#include "oq_sm100.cuh"
+
+#include <mutex>
+#include <set>
 
 namespace oq {
 
@@ -25,6 +28,7 @@ template <> struct XTraits<__half> {
     }
     static __device__ __forceinline__ float round(float v) { return __half2float(__float2half_rn(v)); }
     static __device__ __forceinline__ float to_f32(__half v) { return __half2float(v); }
+    static __device__ __forceinline__ __half zero() { return __float2half(0.0f); }
     static __device__ __forceinline__ void mma(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                                uint32_t b0, uint32_t b1) {
         asm volatile(
@@ -41,6 +45,7 @@ template <> struct XTraits<__nv_bfloat16> {
     }
     static __device__ __forceinline__ float round(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
     static __device__ __forceinline__ float to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
+    static __device__ __forceinline__ __nv_bfloat16 zero() { return __float2bfloat16(0.0f); }
     static __device__ __forceinline__ void mma(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                                uint32_t b0, uint32_t b1) {
         asm volatile(
@@ -58,61 +63,60 @@ __device__ __forceinline__ float dq(uint32_t word, int i, float s) {
     return __fmul_rn(__fsub_rn(f, 8388616.0f), s);                               // (u - 8) * s
 }
 
-// Per-(row, group) multipliers of dq_word: s * 16^-p for the nibble
-// positions p the word is split into, and -8s.
+// Per-(row, group) constants of dq_half: s and s * 16^-1 for nibble
+// positions 0 and 1, s * 16^-2 and s * 16^-3 for positions 2 and 3, and -8s.
 struct DqScale {
-    float2 mul[4];
-    float2 m8s;
-    bool fast;  // s * 2^-16 is a normal float and 8s is finite
+    float2 mul01, mul23, m8s;
+    float s;
+    bool fast;  // s * 16^-3 is a normal float and 8s is finite
 };
 
 __device__ __forceinline__ DqScale make_dq_scale(float s) {
     DqScale d;
-    const float s4 = s * 0.0625f, s8 = s * 0.00390625f, s12 = s * 0.000244140625f, s16 = s * 1.52587890625e-05f;
-    d.mul[0] = make_float2(s, s4);
-    d.mul[1] = make_float2(s8, s12);
-    d.mul[2] = make_float2(s16, s8);
-    d.mul[3] = make_float2(s12, s16);
+    d.s = s;
+    d.mul01 = make_float2(s, s * 0.0625f);
+    d.mul23 = make_float2(s * 0.00390625f, s * 0.000244140625f);
     d.m8s = make_float2(-8.0f * s, -8.0f * s);
     const float a = fabsf(s);
     d.fast = (a >= 0x1p-100f && a <= 0x1p100f);
     return d;
 }
 
-// Eight weights of one packed word (raw two's-complement nibbles, element i
-// in bits 4i..4i+3) -> four packed pairs {w(2j), w(2j+1)} of
-// round_x(fl32(q * s)).  The nibbles are lifted into fp32 as 2^23 + u*16^p
-// (u = q + 8, offset binary, p = the nibble's position after at most one
-// 12-bit shift) by AND/XOR into the 0x4B000000 exponent; subtracting 2^23 is
-// exact, and fma(u*16^p, s*16^-p, -8s) is the exact value (u - 8) * s = q * s
-// rounded once -- the reference's fp32 product.  Blackwell's packed
-// f32x2 add/fma do two weights per instruction.  Scales whose 16^-4 multiple
-// would be subnormal (or non-finite) take the per-nibble path.
-template <typename XT>
-__device__ __forceinline__ void dq_word(uint32_t w, const DqScale &sc, float s, uint32_t (&h)[4]) {
-    if (sc.fast) {
-        const uint32_t wh = w >> 12;
-        const float f0 = __uint_as_float((w & 0x0000000Fu) ^ 0x4B000008u);
-        const float f1 = __uint_as_float((w & 0x000000F0u) ^ 0x4B000080u);
-        const float f2 = __uint_as_float((w & 0x00000F00u) ^ 0x4B000800u);
-        const float f3 = __uint_as_float((w & 0x0000F000u) ^ 0x4B008000u);
-        const float f4 = __uint_as_float((w & 0x000F0000u) ^ 0x4B080000u);
-        const float f5 = __uint_as_float((wh & 0x00000F00u) ^ 0x4B000800u);
-        const float f6 = __uint_as_float((wh & 0x0000F000u) ^ 0x4B008000u);
-        const float f7 = __uint_as_float((wh & 0x000F0000u) ^ 0x4B080000u);
+// Four weights -- nibbles 4*H .. 4*H+3 of a packed word (raw two's-complement
+// nibbles, element i in bits 4i..4i+3) -> two packed pairs
+// {w(2j), w(2j+1)} of round_x(fl32(q * s)).  The word is shifted so the four
+// nibbles sit at positions p = 0..3; each is lifted into fp32 as
+// 2^23 + u*16^p (u = q + 8, offset binary) by one AND/XOR into the 0x4B000000
+// exponent; subtracting 2^23 is exact, and fma(u*16^p, s*16^-p, -8s) is the
+// exact value (u - 8) * s = q * s rounded once -- the reference's fp32
+// product.  Blackwell's packed f32x2 add/fma do two weights per instruction.
+// Scales whose 16^-3 multiple would be subnormal (or non-finite) take the
+// per-nibble path.
+// (a & b) ^ c in one LOP3 (truth table 0x6A); the compiler otherwise emits
+// an AND and an XOR, and the ALU pipe is this kernel's limit.
+__device__ __forceinline__ float and_xor_f(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d;
+    asm("lop3.b32 %0, %1, %2, %3, 0x6A;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return __uint_as_float(d);
+}
+
+template <typename XT, int H, bool FAST>
+__device__ __forceinline__ void dq_half(uint32_t w, const DqScale &sc, uint32_t (&h)[2]) {
+    if (FAST) {
+        const uint32_t v = H ? (w >> 16) : w;
+        const float f0 = and_xor_f(v, 0x000Fu, 0x4B000008u);
+        const float f1 = and_xor_f(v, 0x00F0u, 0x4B000080u);
+        const float f2 = and_xor_f(v, 0x0F00u, 0x4B000800u);
+        const float f3 = and_xor_f(v, 0xF000u, 0x4B008000u);
         const float2 m23 = make_float2(-8388608.0f, -8388608.0f);
-        const float2 w01 = __ffma2_rn(__fadd2_rn(make_float2(f0, f1), m23), sc.mul[0], sc.m8s);
-        const float2 w23 = __ffma2_rn(__fadd2_rn(make_float2(f2, f3), m23), sc.mul[1], sc.m8s);
-        const float2 w45 = __ffma2_rn(__fadd2_rn(make_float2(f4, f5), m23), sc.mul[2], sc.m8s);
-        const float2 w67 = __ffma2_rn(__fadd2_rn(make_float2(f6, f7), m23), sc.mul[3], sc.m8s);
+        const float2 w01 = __ffma2_rn(__fadd2_rn(make_float2(f0, f1), m23), sc.mul01, sc.m8s);
+        const float2 w23 = __ffma2_rn(__fadd2_rn(make_float2(f2, f3), m23), sc.mul23, sc.m8s);
         h[0] = XTraits<XT>::pack(w01.x, w01.y);
         h[1] = XTraits<XT>::pack(w23.x, w23.y);
-        h[2] = XTraits<XT>::pack(w45.x, w45.y);
-        h[3] = XTraits<XT>::pack(w67.x, w67.y);
     } else {
         const uint32_t u = w ^ 0x88888888u;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) h[j] = XTraits<XT>::pack(dq(u, 2 * j, s), dq(u, 2 * j + 1, s));
+        h[0] = XTraits<XT>::pack(dq(u, 4 * H, sc.s), dq(u, 4 * H + 1, sc.s));
+        h[1] = XTraits<XT>::pack(dq(u, 4 * H + 2, sc.s), dq(u, 4 * H + 3, sc.s));
     }
 }
 
@@ -134,121 +138,515 @@ __device__ __forceinline__ void dq_word(uint32_t w, const DqScale &sc, float s, 
 // k-slots {2t, 2t+1, 2t+8, 2t+9} of a lane carry four consecutive real
 // columns of its own segment, and B is loaded with the same permutation, so
 // the tensor-core sum over slots is the sum over real columns.  NT n-tiles
-// cover M <= 8*NT.  x is staged in shared memory when it fits (XS).
-template <typename XT, int NT, int WARPS, int U, bool XS>
-__global__ void __launch_bounds__(WARPS * 32) gemv_int4_kernel(const XT *__restrict__ x,
-                                                               const uint8_t *__restrict__ packed,
-                                                               const float *__restrict__ scales,
-                                                               float *__restrict__ y, int m, int64_t n, int64_t k,
-                                                               int64_t kp, int g) {
-    extern __shared__ uint4 xs_raw[];
-    __shared__ float red[WARPS][NT][4][32];
-    const XT *xs = reinterpret_cast<const XT *>(xs_raw);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int gi = lane >> 2, t = lane & 3;
-    const int64_t row0 = (int64_t)blockIdx.x * 16;
-    const int64_t ra = row0 + gi, rb = row0 + gi + 8;
-    const bool va = ra < n, vb = rb < n;
-    const int64_t groups = kp / g;
-    const int64_t nchunks = cdiv(kp, 128);
-    const uint8_t *pa = packed + ra * (kp / 2);
-    const uint8_t *pb = packed + rb * (kp / 2);
-    const float *sra = scales + ra * groups;
-    const float *srb = scales + rb * groups;
-
-    uint4 wa[U], wb[U];
-    float sa[U], sb[U];
-    auto load = [&](int u, int64_t c) {
-        const int64_t k0 = 128 * c + 32 * t;
-        wa[u] = make_uint4(0, 0, 0, 0);
-        wb[u] = make_uint4(0, 0, 0, 0);
-        sa[u] = 0.0f;
-        sb[u] = 0.0f;
-        if (c < nchunks && k0 < kp) {
-            if (va) {
-                wa[u] = __ldg(reinterpret_cast<const uint4 *>(pa + k0 / 2));
-                sa[u] = __ldg(sra + k0 / g);
-            }
-            if (vb) {
-                wb[u] = __ldg(reinterpret_cast<const uint4 *>(pb + k0 / 2));
-                sb[u] = __ldg(srb + k0 / g);
+// cover M <= 8*NT.
+//
+// The inner loop carries no bounds logic: rows past N are clamped to row N-1
+// (their outputs are never stored), prefetches past the last chunk are
+// clamped to it, lane segments past KP read column 0 with a zero scale, and
+// x is either staged in shared memory zero-padded to 128*nchunks columns
+// (XS) or, when it is too large, read from global memory (then KP == K and
+// KP % 128 == 0 are required).  Batch lanes >= M keep zero B fragments via
+// predicated loads into registers zeroed once.
+// One 128-column chunk of the GEMV: for each of the lane's four words, the
+// B fragment (x) and the two k16 steps of dequant + mma.
+template <typename XT, int NT, bool XS, bool FAST>
+__device__ __forceinline__ void gemv_chunk(int c, const uint32_t (&qa)[4], const uint32_t (&qb)[4],
+                                           const DqScale &dsa, const DqScale &dsb, const uint32_t (&xaddr)[NT],
+                                           const bool (&xon)[NT], const XT *const (&xg)[NT], uint4 (&xb)[NT],
+                                           float (&acc)[2][NT][4]) {
+#pragma unroll
+    for (int wd = 0; wd < 4; ++wd) {
+#pragma unroll
+        for (int j = 0; j < NT; ++j) {
+            if (XS) {
+                const uint32_t addr = xaddr[j] + (uint32_t)(128 * c + 8 * wd) * 2u;
+                asm volatile(
+                    "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+                    " @p ld.shared.v4.u32 {%0, %1, %2, %3}, [%5];\n}\n"
+                    : "+r"(xb[j].x), "+r"(xb[j].y), "+r"(xb[j].z), "+r"(xb[j].w)
+                    : "r"((int)xon[j]), "r"(addr));
+            } else if (xon[j]) {
+                xb[j] = __ldg(reinterpret_cast<const uint4 *>(xg[j] + 128 * c + 8 * wd));
             }
         }
-    };
+        // k16 step 0: nibbles 0-3 (pairs 0, 1); step 1: nibbles 4-7.
+        {
+            uint32_t ha[2], hb[2];
+            dq_half<XT, 0, FAST>(qa[wd], dsa, ha);
+            dq_half<XT, 0, FAST>(qb[wd], dsb, hb);
 #pragma unroll
-    for (int u = 0; u < U; ++u) load(u, warp + (int64_t)u * WARPS);
+            for (int j = 0; j < NT; ++j)
+                XTraits<XT>::mma(acc[0][j], ha[0], hb[0], ha[1], hb[1], xb[j].x, xb[j].y);
+        }
+        {
+            uint32_t ha[2], hb[2];
+            dq_half<XT, 1, FAST>(qa[wd], dsa, ha);
+            dq_half<XT, 1, FAST>(qb[wd], dsb, hb);
+#pragma unroll
+            for (int j = 0; j < NT; ++j)
+                XTraits<XT>::mma(acc[1][j], ha[0], hb[0], ha[1], hb[1], xb[j].z, xb[j].w);
+        }
+    }
+}
+
+// Bytes of the GEMV's double-buffered cross-warp reduction buffer.
+__host__ __device__ constexpr size_t gemv_red_bytes(int warps, int nt) { return 2u * warps * nt * 4 * 32 * 4; }
+
+// Scale-after variant of gemv_chunk (fp16 x, whole 128-column chunk in one
+// group): nibbles become exact fp16 integers and the group scale is applied
+// to the chunk's fp32 partial sums.  Per packed word W the LOP3 magic
+// (W & 0x000F000F) ^ 0x64086408 is the half pair (1024 + u0, 1024 + u4),
+// u = n ^ 8 the offset-binary nibble; the 0x00F000F0 mask gives
+// (1024 + 16 u1, 1024 + 16 u5), and W >> 8 the same for nibbles 2, 6 and 3,
+// 7.  One HSUB2 of 1032 (or 1024 + 128) leaves q (or 16 q) exactly.  The
+// "class 0" k16 step takes nibbles {0,4,2,6}, the "class 1" step nibbles
+// {1,5,3,7} (16 q); x is staged in the matching order, so one 16-byte load
+// gives both steps' B fragments.  Products of fp16 q and x are exact and the
+// tensor core sums them in fp32; y += s * (sum0 + sum1 / 16) per chunk.
+__device__ __forceinline__ uint32_t lop3_and_xor(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d;
+    asm("lop3.b32 %0, %1, %2, %3, 0x6A;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+__device__ __forceinline__ uint32_t hsub2_u32(uint32_t a, uint32_t b) {
+    __half2 r = __hsub2(*reinterpret_cast<__half2 *>(&a), *reinterpret_cast<__half2 *>(&b));
+    return *reinterpret_cast<uint32_t *>(&r);
+}
+
+template <int NT, bool XS>
+__device__ __forceinline__ void gemv_chunk_sa(int c, const uint32_t (&qa)[4], const uint32_t (&qb)[4], float sa,
+                                              float sb, const uint32_t (&xaddr)[NT], const bool (&xon)[NT],
+                                              const __half *const (&xg)[NT], uint4 (&xb)[NT],
+                                              float (&acc)[2][NT][4]) {
+    float part[4][NT][4];
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int j = 0; j < NT; ++j) part[a][j][0] = part[a][j][1] = part[a][j][2] = part[a][j][3] = 0.0f;
+    const uint32_t k1032 = 0x64086408u;  // half2 (1032, 1032)
+    const uint32_t k1152 = 0x64806480u;  // half2 (1152, 1152)
+#pragma unroll
+    for (int wd = 0; wd < 4; ++wd) {
+#pragma unroll
+        for (int j = 0; j < NT; ++j) {
+            if (XS) {
+                const uint32_t addr = xaddr[j] + (uint32_t)(128 * c + 8 * wd) * 2u;
+                asm volatile(
+                    "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+                    " @p ld.shared.v4.u32 {%0, %1, %2, %3}, [%5];\n}\n"
+                    : "+r"(xb[j].x), "+r"(xb[j].y), "+r"(xb[j].z), "+r"(xb[j].w)
+                    : "r"((int)xon[j]), "r"(addr));
+            } else if (xon[j]) {
+                // natural order x0..x7 -> (x0,x4) (x2,x6) (x1,x5) (x3,x7)
+                const uint4 v = __ldg(reinterpret_cast<const uint4 *>(xg[j] + 128 * c + 8 * wd));
+                xb[j].x = __byte_perm(v.x, v.z, 0x5410);
+                xb[j].y = __byte_perm(v.y, v.w, 0x5410);
+                xb[j].z = __byte_perm(v.x, v.z, 0x7632);
+                xb[j].w = __byte_perm(v.y, v.w, 0x7632);
+            }
+        }
+        const uint32_t wa = qa[wd], wb = qb[wd];
+        const uint32_t wa8 = wa >> 8, wb8 = wb >> 8;
+        // class 0: (q0, q4) and (q2, q6)
+        {
+            const uint32_t a0 = hsub2_u32(lop3_and_xor(wa, 0x000F000Fu, 0x64086408u), k1032);
+            const uint32_t a2 = hsub2_u32(lop3_and_xor(wa8, 0x000F000Fu, 0x64086408u), k1032);
+            const uint32_t b0 = hsub2_u32(lop3_and_xor(wb, 0x000F000Fu, 0x64086408u), k1032);
+            const uint32_t b2 = hsub2_u32(lop3_and_xor(wb8, 0x000F000Fu, 0x64086408u), k1032);
+#pragma unroll
+            for (int j = 0; j < NT; ++j)
+                XTraits<__half>::mma(part[wd & 1][j], a0, b0, a2, b2, xb[j].x, xb[j].y);
+        }
+        // class 1: (16 q1, 16 q5) and (16 q3, 16 q7)
+        {
+            const uint32_t a1 = hsub2_u32(lop3_and_xor(wa, 0x00F000F0u, 0x64806480u), k1152);
+            const uint32_t a3 = hsub2_u32(lop3_and_xor(wa8, 0x00F000F0u, 0x64806480u), k1152);
+            const uint32_t b1 = hsub2_u32(lop3_and_xor(wb, 0x00F000F0u, 0x64806480u), k1152);
+            const uint32_t b3 = hsub2_u32(lop3_and_xor(wb8, 0x00F000F0u, 0x64806480u), k1152);
+#pragma unroll
+            for (int j = 0; j < NT; ++j)
+                XTraits<__half>::mma(part[2 + (wd & 1)][j], a1, b1, a3, b3, xb[j].z, xb[j].w);
+        }
+    }
+    // D fragment: elements 0, 1 belong to row g (scale sa), 2, 3 to row g+8.
+    const float sa16 = sa * 0.0625f, sb16 = sb * 0.0625f;
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+        acc[0][j][0] = fmaf(part[0][j][0] + part[1][j][0], sa, acc[0][j][0]);
+        acc[0][j][1] = fmaf(part[0][j][1] + part[1][j][1], sa, acc[0][j][1]);
+        acc[0][j][2] = fmaf(part[0][j][2] + part[1][j][2], sb, acc[0][j][2]);
+        acc[0][j][3] = fmaf(part[0][j][3] + part[1][j][3], sb, acc[0][j][3]);
+        acc[1][j][0] = fmaf(part[2][j][0] + part[3][j][0], sa16, acc[1][j][0]);
+        acc[1][j][1] = fmaf(part[2][j][1] + part[3][j][1], sa16, acc[1][j][1]);
+        acc[1][j][2] = fmaf(part[2][j][2] + part[3][j][2], sb16, acc[1][j][2]);
+        acc[1][j][3] = fmaf(part[2][j][3] + part[3][j][3], sb16, acc[1][j][3]);
+    }
+}
+
+template <typename XT, int NT, int WARPS, int U, bool XS, int MINB, bool SA>
+__global__ void __launch_bounds__(WARPS * 32, MINB) gemv_int4_kernel(const XT *__restrict__ x,
+                                                               const uint8_t *__restrict__ packed,
+                                                               const float *__restrict__ scales,
+                                                               float *__restrict__ y, int m, int n, int k, int kp,
+                                                               int gshift, int xstride) {
+    static_assert(!SA || std::is_same<XT, __half>::value, "scale-after mode is for fp16 x");
+    // Dynamic shared memory: the double-buffered cross-warp reduction, then
+    // the staged x.
+    extern __shared__ uint4 smem_dyn[];
+    auto red = reinterpret_cast<float(*)[WARPS][NT][4][32]>(smem_dyn);
+    uint4 *xs_raw = smem_dyn + gemv_red_bytes(WARPS, NT) / 16;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int gi = lane >> 2, t = lane & 3;
+    const int nchunks = (kp + 127) >> 7;
+    const int groups = kp >> gshift;
+    const int tiles = (n + 15) >> 4;
+    // This CTA's tiles: blockIdx.x, blockIdx.x + gridDim.x, ...; each warp
+    // walks positions p = (tile i, its j-th chunk c = warp + j * WARPS).
+    const int my_tiles = blockIdx.x < tiles ? (tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    const int cpw = (nchunks + WARPS - 1) / WARPS;  // chunk slots per warp per tile
+    const int npos = my_tiles * cpw;
+
+    // Refill cursor: the next position to load, as (tile ordinal, slot)
+    // with row pointers recomputed only when the tile changes.
+    int r_ti = 0, r_jj = 0;
+    const uint8_t *r_pa = nullptr, *r_pb = nullptr;
+    const float *r_sa = nullptr, *r_sb = nullptr;
+    auto set_rows = [&](int ti) {
+        const int row0 = ((int)blockIdx.x + ti * (int)gridDim.x) * 16;
+        const int ra = min(row0 + gi, n - 1), rb = min(row0 + gi + 8, n - 1);
+        r_pa = packed + (size_t)ra * (kp / 2) + 16 * t;
+        r_pb = packed + (size_t)rb * (kp / 2) + 16 * t;
+        r_sa = scales + (size_t)ra * groups;
+        r_sb = scales + (size_t)rb * groups;
+    };
+    uint4 wa[U], wb[U];
+    float sa[U], sb[U];
+    // Loads the cursor's chunk into slot u and advances the cursor (past the
+    // last position it keeps re-reading the last chunk, which is harmless).
+    auto load = [&](int u) {
+        const int c = min(warp + r_jj * WARPS, nchunks - 1);
+        const int k0 = 128 * c + 32 * t;
+        const bool in = k0 < kp;
+        const int off = in ? 64 * c : -16 * t;
+        const int sidx = in ? (k0 >> gshift) : 0;
+        wa[u] = __ldg(reinterpret_cast<const uint4 *>(r_pa + off));
+        wb[u] = __ldg(reinterpret_cast<const uint4 *>(r_pb + off));
+        const float a = __ldg(r_sa + sidx);
+        const float b = __ldg(r_sb + sidx);
+        sa[u] = in ? a : 0.0f;
+        sb[u] = in ? b : 0.0f;
+        if (++r_jj == cpw && r_ti + 1 < my_tiles) {
+            r_jj = 0;
+            set_rows(++r_ti);
+        } else if (r_jj == cpw) {
+            r_jj = cpw - 1;  // stay on the last position
+        }
+    };
+    if (npos > 0) {
+        set_rows(0);
+#pragma unroll
+        for (int u = 0; u < U; ++u) load(u);
+    }
 
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;");
+    if (npos == 0) return;
 
-    if (XS) {  // stage x [m][k] (k % 8 == 0) in shared memory
-        const int64_t vecs = (int64_t)m * k / 8;
-        for (int64_t i = threadIdx.x; i < vecs; i += blockDim.x)
-            xs_raw[i] = __ldg(reinterpret_cast<const uint4 *>(x) + i);
+    if (XS) {  // x [m][k] -> xs [m][xstride] halves, zero beyond k
+        const int rowv = xstride / 8, kv = k / 8;
+        for (int i = threadIdx.x; i < m * rowv; i += blockDim.x) {
+            const int r = i / rowv, c = i - r * rowv;
+            uint4 v = c < kv ? __ldg(reinterpret_cast<const uint4 *>(x) + (size_t)r * kv + c) : make_uint4(0, 0, 0, 0);
+            if (SA) {  // x0..x7 -> (x0,x4) (x2,x6) (x1,x5) (x3,x7)
+                v = make_uint4(__byte_perm(v.x, v.z, 0x5410), __byte_perm(v.y, v.w, 0x5410),
+                               __byte_perm(v.x, v.z, 0x7632), __byte_perm(v.y, v.w, 0x7632));
+            }
+            xs_raw[i] = v;
+        }
         __syncthreads();
     }
-
-    float acc[NT][4];
+    // Per n-tile: this lane's batch row and whether it exists.
+    uint32_t xaddr[NT];
+    bool xon[NT];
+    const XT *xg[NT];
 #pragma unroll
-    for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
+    for (int j = 0; j < NT; ++j) {
+        const int mb = 8 * j + gi;
+        xon[j] = mb < m;
+        const int mr = xon[j] ? mb : 0;
+        xaddr[j] = (uint32_t)__cvta_generic_to_shared(xs_raw) + (uint32_t)(mr * xstride + 32 * t) * 2u;
+        xg[j] = x + (size_t)mr * k + 32 * t;
+    }
+    uint4 xb[NT];
+#pragma unroll
+    for (int j = 0; j < NT; ++j) xb[j] = make_uint4(0, 0, 0, 0);
 
-    const int64_t mine = nchunks > warp ? cdiv(nchunks - warp, WARPS) : 0;  // chunks of this warp
-    for (int64_t base = 0; base < mine; base += U) {
+    // Two accumulator sets (even / odd k16 step) halve the mma dependency chain.
+    float acc[2][NT][4];
+#pragma unroll
+    for (int a = 0; a < 2; ++a)
+#pragma unroll
+        for (int j = 0; j < NT; ++j) acc[a][j][0] = acc[a][j][1] = acc[a][j][2] = acc[a][j][3] = 0.0f;
+
+    // Compute cursor: tile ordinal ti, slot jj (chunk c = warp + jj * WARPS).
+    int ti = 0, jj = 0;
+    for (int base = 0; base < npos; base += U) {
 #pragma unroll
         for (int u = 0; u < U; ++u) {
-            const int64_t c = warp + (base + u) * WARPS;
-            if (base + u < mine) {
-                const int k0 = (int)(128 * c + 32 * t);
-                const uint32_t qa[4] = {wa[u].x, wa[u].y, wa[u].z, wa[u].w};
-                const uint32_t qb[4] = {wb[u].x, wb[u].y, wb[u].z, wb[u].w};
-                const DqScale dsa = make_dq_scale(sa[u]), dsb = make_dq_scale(sb[u]);
-#pragma unroll
-                for (int wd = 0; wd < 4; ++wd) {
-                    const int kw = k0 + 8 * wd;  // columns kw..kw+7
-                    uint4 xb[NT];
-#pragma unroll
-                    for (int j = 0; j < NT; ++j) {
-                        const int mb = 8 * j + gi;
-                        if (mb < m && kw < k)
-                            xb[j] = XS ? *reinterpret_cast<const uint4 *>(xs + mb * (int)k + kw)
-                                       : __ldg(reinterpret_cast<const uint4 *>(x + (int64_t)mb * k + kw));
+            if (base + u < npos) {
+                const int c = warp + jj * WARPS;
+                if (c < nchunks) {
+                    const uint32_t qa[4] = {wa[u].x, wa[u].y, wa[u].z, wa[u].w};
+                    const uint32_t qb[4] = {wb[u].x, wb[u].y, wb[u].z, wb[u].w};
+                    if constexpr (SA) {
+                        gemv_chunk_sa<NT, XS>(c, qa, qb, sa[u], sb[u], xaddr, xon, xg, xb, acc);
+                    } else {
+                        // One warp-uniform branch per chunk keeps the rare
+                        // per-nibble path out of the hot loop.
+                        const DqScale dsa = make_dq_scale(sa[u]), dsb = make_dq_scale(sb[u]);
+                        if (__all_sync(0xffffffffu, dsa.fast && dsb.fast))
+                            gemv_chunk<XT, NT, XS, true>(c, qa, qb, dsa, dsb, xaddr, xon, xg, xb, acc);
                         else
-                            xb[j] = make_uint4(0, 0, 0, 0);
-                    }
-                    uint32_t ha[4], hb[4];
-                    dq_word<XT>(qa[wd], dsa, sa[u], ha);
-                    dq_word<XT>(qb[wd], dsb, sb[u], hb);
-                    // k16 step 0: nibbles 0-3 (pairs 0, 1); step 1: nibbles 4-7.
-#pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-#pragma unroll
-                        for (int j = 0; j < NT; ++j) {
-                            const uint32_t b0 = h == 0 ? xb[j].x : xb[j].z;
-                            const uint32_t b1 = h == 0 ? xb[j].y : xb[j].w;
-                            XTraits<XT>::mma(acc[j], ha[2 * h], hb[2 * h], ha[2 * h + 1], hb[2 * h + 1], b0, b1);
-                        }
+                            gemv_chunk<XT, NT, XS, false>(c, qa, qb, dsa, dsb, xaddr, xon, xg, xb, acc);
                     }
                 }
+                load(u);  // refill the slot: the next tile's chunks stream in
+                if (++jj == cpw) {
+                    // End of this CTA's tile ti: fixed-order reduction over warps.
+                    const int buf = ti & 1;
+#pragma unroll
+                    for (int j = 0; j < NT; ++j)
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            red[buf][warp][j][e][lane] = acc[0][j][e] + acc[1][j][e];
+                            acc[0][j][e] = 0.0f;
+                            acc[1][j][e] = 0.0f;
+                        }
+                    __syncthreads();
+                    const int row0 = ((int)blockIdx.x + ti * (int)gridDim.x) * 16;
+                    for (int idx = threadIdx.x; idx < NT * 4 * 32; idx += blockDim.x) {
+                        const int j = idx / 128, e = (idx / 32) % 4, ln = idx % 32;
+                        float v = 0.0f;
+#pragma unroll
+                        for (int wv = 0; wv < WARPS; ++wv) v += red[buf][wv][j][e][ln];
+                        const int g2 = ln >> 2, t2 = ln & 3;
+                        const int row = row0 + g2 + (e >= 2 ? 8 : 0);
+                        const int mb = 8 * j + 2 * t2 + (e & 1);
+                        if (row < n && mb < m) y[(size_t)mb * n + row] = v;
+                    }
+                    jj = 0;
+                    ++ti;
+                }
             }
-            load(u, warp + (base + u + U) * WARPS);  // refill the slot
         }
     }
+}
 
-#pragma unroll
-    for (int j = 0; j < NT; ++j)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) red[warp][j][e][lane] = acc[j][e];
+// ----------------------------------------------------------- TMA GEMV ----
+//
+// Persistent decode GEMV fed by TMA.  One CTA per SM loops over 16-row
+// tiles; a tile's K is cut into stages of 128*CPW*CW columns (32 KB of
+// packed weights: fewer, larger stages stream faster than many small ones).
+// Warp CW (the producer) keeps a ring of S stages in flight: for each stage
+// it waits for the slot to be empty, then one lane issues the stage's TMA
+// boxes (16 rows x 128 bytes each, 128-byte swizzled) and, when the scales'
+// row pitch allows it (groups % 4 == 0), one TMA box of the stage's scales,
+// all completing on full[slot].  Consumer warp w takes the stage's chunks
+// w, w + CW, ... (128 columns each): it reads its two 16-byte pieces per
+// chunk (rows g and g+8) from the swizzled boxes conflict-free, runs the
+// same dequant + mma as the register-ring kernel, and arrives on
+// empty[slot].  At the end of a tile the consumer warps reduce their partial
+// sums in a fixed order (named barrier 1, producer excluded).
+//
+// Everything the producer streams is read-only, so it starts before
+// griddepcontrol.wait; the consumers read x and write y after it.
+template <int CW, int CPW>
+struct TmaGemvLayout {
+    static constexpr int kStageCols = 128 * CW * CPW;  // columns per stage
+    static constexpr int kStageBytes = 16 * kStageCols / 2;
+    static constexpr int kBoxes = kStageBytes / 2048;  // 16 rows x 128 B boxes
+};
+
+template <typename XT, int NT, int CW, int CPW, bool SA, bool XS, bool STMA>
+__global__ void __launch_bounds__((CW + 1) * 32, CW <= 8 ? 2 : 1)
+    gemv_tma_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap smap,
+                    const XT *__restrict__ x, const float *__restrict__ scales, float *__restrict__ y, int m, int n,
+                    int k, int kp, int gshift, int xstride, int nstages) {
+    static_assert(!SA || std::is_same<XT, __half>::value, "scale-after mode is for fp16 x");
+    using L = TmaGemvLayout<CW, CPW>;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    // 1024-byte alignment for the swizzled boxes.
+    uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+    const int spr = L::kStageCols >> gshift;  // scales per row per stage
+    const int sbytes = ((16 * spr * 4 + 127) / 128) * 128;
+    uint8_t *wbuf = smem;                                               // [S][boxes][16][128]
+    float *sbuf = reinterpret_cast<float *>(wbuf + (size_t)nstages * L::kStageBytes);  // [S][16][spr]
+    uint64_t *full = reinterpret_cast<uint64_t *>(reinterpret_cast<uint8_t *>(sbuf) + (size_t)nstages * sbytes);
+    uint64_t *empty = full + nstages;
+    auto red = reinterpret_cast<float(*)[CW][NT][4][32]>(empty + nstages);  // [2]
+    XT *xs = reinterpret_cast<XT *>(reinterpret_cast<uint8_t *>(red) + gemv_red_bytes(CW, NT));
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int groups = kp >> gshift;
+    const int tiles = (n + 15) >> 4;
+    const int my_tiles = (int)blockIdx.x < tiles ? (tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    const int nchunks = (kp + 127) >> 7;
+    const int spt = (kp + L::kStageCols - 1) / L::kStageCols;  // stages per tile
+    const int npos = my_tiles * spt;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < nstages; ++i) {
+            mbar_init(&full[i], 1);   // the producer's expect_tx arrival
+            mbar_init(&empty[i], CW);  // one arrival per consumer warp
+        }
+        fence_barrier_init();
+    }
     __syncthreads();
-    // Fixed-order reduction over warps; thread (j, e, lane) owns one output.
-    for (int idx = threadIdx.x; idx < NT * 4 * 32; idx += blockDim.x) {
-        const int j = idx / 128, e = (idx / 32) % 4, ln = idx % 32;
-        float v = 0.0f;
+
+    if (warp == CW) {  // ------------------------------------ producer
+        if (lane == 0) {
+            tma_prefetch_desc(&wmap);
+            if (STMA) tma_prefetch_desc(&smap);
+            for (int pos = 0; pos < npos; ++pos) {
+                const int slot = pos % nstages, round = pos / nstages;
+                if (round > 0 && !mbar_wait(&empty[slot], (round - 1) & 1)) break;
+                const int ti = pos / spt, st = pos - ti * spt;
+                const int row0 = ((int)blockIdx.x + ti * (int)gridDim.x) * 16;
+                const int k0 = st * L::kStageCols;
+                mbar_arrive_expect_tx(&full[slot], L::kStageBytes + (STMA ? 16 * spr * 4 : 0));
 #pragma unroll
-        for (int wv = 0; wv < WARPS; ++wv) v += red[wv][j][e][ln];
-        const int g2 = ln >> 2, t2 = ln & 3;
-        const int64_t row = row0 + g2 + (e >= 2 ? 8 : 0);
-        const int mb = 8 * j + 2 * t2 + (e & 1);
-        if (row < n && mb < m) y[(int64_t)mb * n + row] = v;
+                for (int b = 0; b < L::kBoxes; ++b)
+                    tma_load_2d(wbuf + (size_t)slot * L::kStageBytes + b * 2048, &wmap, &full[slot], k0 / 2 + 128 * b,
+                                row0);
+                if (STMA)
+                    tma_load_2d(reinterpret_cast<uint8_t *>(sbuf) + (size_t)slot * sbytes, &smap, &full[slot],
+                                k0 >> gshift, row0);
+            }
+        }
+        return;
+    }
+
+    // ------------------------------------------------------ consumers
+    const int gi = lane >> 2, t = lane & 3;
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;");
+    if (XS) {  // x [m][k] -> xs [m][xstride], zero beyond k (SA: pair-permuted)
+        const int rowv = xstride / 8, kv = k / 8;
+        for (int i = threadIdx.x; i < m * rowv; i += CW * 32) {
+            const int r = i / rowv, c = i - r * rowv;
+            uint4 v = c < kv ? __ldg(reinterpret_cast<const uint4 *>(x) + (size_t)r * kv + c) : make_uint4(0, 0, 0, 0);
+            if (SA)
+                v = make_uint4(__byte_perm(v.x, v.z, 0x5410), __byte_perm(v.y, v.w, 0x5410),
+                               __byte_perm(v.x, v.z, 0x7632), __byte_perm(v.y, v.w, 0x7632));
+            reinterpret_cast<uint4 *>(xs)[i] = v;
+        }
+        asm volatile("bar.sync 1, %0;" ::"r"(CW * 32) : "memory");
+    }
+    uint32_t xaddr[NT];
+    bool xon[NT];
+    const XT *xg[NT];
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+        const int mb = 8 * j + gi;
+        xon[j] = mb < m;
+        const int mr = xon[j] ? mb : 0;
+        xaddr[j] = smem_u32(xs) + (uint32_t)(mr * xstride + 32 * t) * 2u;
+        xg[j] = x + (size_t)mr * k + 32 * t;
+    }
+    uint4 xb[NT];
+#pragma unroll
+    for (int j = 0; j < NT; ++j) xb[j] = make_uint4(0, 0, 0, 0);
+    float acc[2][NT][4];
+#pragma unroll
+    for (int a = 0; a < 2; ++a)
+#pragma unroll
+        for (int j = 0; j < NT; ++j) acc[a][j][0] = acc[a][j][1] = acc[a][j][2] = acc[a][j][3] = 0.0f;
+
+    bool ok = true;
+    int ti = 0, st = 0;
+    for (int pos = 0; pos < npos; ++pos) {
+        const int slot = pos % nstages, round = pos / nstages;
+        const int row0 = ((int)blockIdx.x + ti * (int)gridDim.x) * 16;
+        // Scales without TMA: each lane reads its two rows' scales for its
+        // chunks of this stage straight from global memory.
+        float sreg[CPW][2];
+        if (!STMA) {
+            const int ra = min(row0 + gi, n - 1), rb = min(row0 + gi + 8, n - 1);
+#pragma unroll
+            for (int q = 0; q < CPW; ++q) {
+                const int c = st * CW * CPW + warp + q * CW;
+                const int col = min((128 * c + 32 * t) >> gshift, groups - 1);
+                sreg[q][0] = __ldg(scales + (size_t)ra * groups + col);
+                sreg[q][1] = __ldg(scales + (size_t)rb * groups + col);
+            }
+        }
+        if (ok) ok = mbar_wait(&full[slot], round & 1);
+        if (ok) {
+            const uint8_t *wst = wbuf + (size_t)slot * L::kStageBytes;
+            const float *sst = reinterpret_cast<const float *>(reinterpret_cast<const uint8_t *>(sbuf) + (size_t)slot * sbytes);
+            auto do_chunk = [&](int q) {
+                const int cs = warp + q * CW;            // chunk within the stage
+                const int c = st * CW * CPW + cs;        // chunk within the row
+                // Chunk cs = 64 bytes of each row: box cs/2, chunk
+                // ((cs%2)*4 + t) of the 128-byte row, swizzled by row % 8.
+                const uint32_t piece = (uint32_t)(cs >> 1) * 2048u + (uint32_t)gi * 128u +
+                                       (uint32_t)(((((cs & 1) << 2) + t) ^ (gi & 7)) << 4);
+                const uint4 wa = *reinterpret_cast<const uint4 *>(wst + piece);
+                const uint4 wb = *reinterpret_cast<const uint4 *>(wst + piece + 8 * 128);
+                const int scol = (cs * 128 + 32 * t) >> gshift;
+                const float sa = STMA ? sst[gi * spr + scol] : sreg[q][0];
+                const float sb = STMA ? sst[(gi + 8) * spr + scol] : sreg[q][1];
+                const bool in = 128 * c + 32 * t < kp;
+                const uint32_t qa[4] = {wa.x, wa.y, wa.z, wa.w};
+                const uint32_t qb[4] = {wb.x, wb.y, wb.z, wb.w};
+                if constexpr (SA) {
+                    gemv_chunk_sa<NT, XS>(c, qa, qb, in ? sa : 0.0f, in ? sb : 0.0f, xaddr, xon, xg, xb, acc);
+                } else {
+                    const DqScale dsa = make_dq_scale(in ? sa : 0.0f), dsb = make_dq_scale(in ? sb : 0.0f);
+                    if (__all_sync(0xffffffffu, dsa.fast && dsb.fast))
+                        gemv_chunk<XT, NT, XS, true>(c, qa, qb, dsa, dsb, xaddr, xon, xg, xb, acc);
+                    else
+                        gemv_chunk<XT, NT, XS, false>(c, qa, qb, dsa, dsb, xaddr, xon, xg, xb, acc);
+                }
+            };
+            if (st * CW * CPW + (CPW - 1) * CW + warp < nchunks) {
+                // Every chunk of this warp is inside K: no per-chunk branch,
+                // so the chunks' instruction streams can interleave.
+#pragma unroll
+                for (int q = 0; q < CPW; ++q) do_chunk(q);
+            } else {
+#pragma unroll
+                for (int q = 0; q < CPW; ++q)
+                    if (st * CW * CPW + warp + q * CW < nchunks) do_chunk(q);
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
+        if (++st == spt) {
+            const int buf = ti & 1;
+#pragma unroll
+            for (int j = 0; j < NT; ++j)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    red[buf][warp][j][e][lane] = acc[0][j][e] + acc[1][j][e];
+                    acc[0][j][e] = 0.0f;
+                    acc[1][j][e] = 0.0f;
+                }
+            asm volatile("bar.sync 1, %0;" ::"r"(CW * 32) : "memory");
+            for (int idx = threadIdx.x; idx < NT * 4 * 32; idx += CW * 32) {
+                const int j = idx / 128, e = (idx / 32) % 4, ln = idx % 32;
+                float v = 0.0f;
+#pragma unroll
+                for (int wv = 0; wv < CW; ++wv) v += red[buf][wv][j][e][ln];
+                const int g2 = ln >> 2, t2 = ln & 3;
+                const int row = row0 + g2 + (e >= 2 ? 8 : 0);
+                const int mb = 8 * j + 2 * t2 + (e & 1);
+                if (ok && row < n && mb < m) y[(size_t)mb * n + row] = v;
+            }
+            st = 0;
+            ++ti;
+        }
     }
 }
 
@@ -285,13 +683,43 @@ __global__ void __launch_bounds__(256) simt_int4_kernel(const XT *__restrict__ x
     }
 }
 
+// Shared memory per block (opt-in maximum), cached per device.
+inline int max_smem_optin() {
+    static int cached[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return 227 * 1024;
+    if (cached[dev] == 0) {
+        int v = 0;
+        if (cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess || v <= 0)
+            v = 227 * 1024;
+        cached[dev] = v;
+    }
+    return cached[dev];
+}
+
+// Opts a kernel into the device's maximum dynamic shared memory, once per
+// (kernel, device).
+inline int allow_max_smem(const void *kern) {
+    static std::mutex mu;
+    static std::set<std::pair<const void *, int>> done;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (done.count({kern, dev})) return OQ_OK;
+    OQ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem_optin()));
+    done.insert({kern, dev});
+    return OQ_OK;
+}
+
 // Launch with programmatic stream serialization: a GEMV that follows
 // another kernel in the stream may start (and prefetch its weights) while
 // that kernel drains.  Without a preceding PDL-aware kernel it behaves like a
 // normal launch.
 template <typename Kern, typename XT>
 int launch_pdl(Kern kern, unsigned blocks, unsigned threads, size_t smem, cudaStream_t st, const XT *x,
-               const uint8_t *packed, const float *scales, float *y, int m, int64_t n, int64_t k, int64_t kp, int g) {
+               const uint8_t *packed, const float *scales, float *y, int m, int n, int k, int kp, int gshift,
+               int xstride) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(blocks);
     cfg.blockDim = dim3(threads);
@@ -302,7 +730,7 @@ int launch_pdl(Kern kern, unsigned blocks, unsigned threads, size_t smem, cudaSt
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t err = cudaLaunchKernelEx(&cfg, kern, x, packed, scales, y, m, n, k, kp, g);
+    cudaError_t err = cudaLaunchKernelEx(&cfg, kern, x, packed, scales, y, m, n, k, kp, gshift, xstride);
     if (err != cudaSuccess) {
         set_error("int4_linear (GEMV): launch failed: %s", cudaGetErrorString(err));
         return OQ_ERR_CUDA;
@@ -310,27 +738,202 @@ int launch_pdl(Kern kern, unsigned blocks, unsigned threads, size_t smem, cudaSt
     return OQ_OK;
 }
 
-template <typename XT, int NT, int WARPS, int U>
+constexpr size_t kGemvMaxXs = 96 * 1024;  // staged-x limit (two CTAs per SM)
+
+// Bytes of x staged in shared memory (0 = x read from global memory).
+inline size_t gemv_xs_bytes(int64_t m, int64_t kp, int xsize) {
+    const int64_t xstride = cdiv(kp, 128) * 128 + 8;
+    const size_t b = (size_t)(m * xstride * xsize);
+    return b <= kGemvMaxXs ? b : 0;
+}
+
+template <typename XT, int NT, int WARPS, int U, int MINB, bool SA>
 int launch_gemv_t(const XT *x, const uint8_t *packed, const float *scales, float *y, int64_t m, int64_t n,
-                  int64_t k, int64_t kp, int g, cudaStream_t st) {
-    const unsigned blocks = (unsigned)cdiv(n, 16);
-    const size_t xbytes = (size_t)m * (size_t)k * sizeof(XT);
-    if (xbytes <= 48 * 1024 - sizeof(float) * WARPS * NT * 128)
-        return launch_pdl(gemv_int4_kernel<XT, NT, WARPS, U, true>, blocks, WARPS * 32, xbytes, st, x, packed,
-                          scales, y, (int)m, n, k, kp, g);
-    return launch_pdl(gemv_int4_kernel<XT, NT, WARPS, U, false>, blocks, WARPS * 32, 0, st, x, packed, scales, y,
-                      (int)m, n, k, kp, g);
+                  int64_t k, int64_t kp, int gshift, cudaStream_t st) {
+    // Persistent grid: MINB CTAs per SM, each looping over 16-row tiles.
+    const int64_t tiles = cdiv(n, 16);
+    const unsigned blocks = (unsigned)std::min<int64_t>(tiles, (int64_t)sm_count() * MINB);
+    const int xstride = (int)(cdiv(kp, 128) * 128 + 8);
+    const size_t xbytes = gemv_xs_bytes(m, kp, (int)sizeof(XT));
+    const size_t smem = gemv_red_bytes(WARPS, NT) + xbytes;
+    auto kern = xbytes ? gemv_int4_kernel<XT, NT, WARPS, U, true, MINB, SA>
+                       : gemv_int4_kernel<XT, NT, WARPS, U, false, MINB, SA>;
+    const int rc = allow_max_smem(reinterpret_cast<const void *>(kern));
+    if (rc != OQ_OK) return rc;
+    return launch_pdl(kern, blocks, WARPS * 32, smem, st, x, packed, scales, y, (int)m, (int)n, (int)k, (int)kp,
+                      gshift, xstride);
+}
+
+// Stage count and shared-memory bytes of the TMA GEMV, or 0 stages when the
+// shape does not fit.  x is staged in shared memory when that leaves at
+// least 4 stages (*xs_out = 1), else read from global memory, which needs
+// whole stages (KP a multiple of the stage width and K == KP).
+template <int CW, int CPW>
+inline int tma_gemv_plan(int64_t m, int64_t k, int64_t kp, int g, int nt, int xsize, size_t *smem_out,
+                         int *xstride_out, bool *xs_out, int ctas_per_sm = 1, int64_t max_pos = 1 << 30) {
+    using L = TmaGemvLayout<CW, CPW>;
+    if (g < 32 || g > L::kStageCols) return 0;
+    const int64_t xstride = cdiv(kp, 128) * 128 + 8;  // chunks past KP are skipped
+    const int64_t spr = L::kStageCols / g;
+    const size_t sbytes = (size_t)cdiv(16 * spr * 4, 128) * 128;
+    const size_t per_stage = (size_t)L::kStageBytes + sbytes + 16;
+    const size_t cap = (size_t)max_smem_optin() / ctas_per_sm - (ctas_per_sm > 1 ? 1024 : 0);
+    const size_t base = 1024 + gemv_red_bytes(CW, nt);
+    const size_t xbytes = (size_t)(m * xstride * xsize);
+    bool xs = base + xbytes + 3 * per_stage <= cap;
+    if (!xs && !(kp == k && kp % L::kStageCols == 0)) return 0;
+    const size_t fixed = base + (xs ? xbytes : 0);
+    if (fixed + 2 * per_stage > cap) return 0;
+    int stages = (int)std::min<size_t>(8, (cap - fixed) / per_stage);
+    stages = (int)std::max<int64_t>(2, std::min<int64_t>(stages, max_pos));
+    *smem_out = fixed + stages * per_stage;
+    *xstride_out = (int)xstride;
+    *xs_out = xs;
+    return stages;
+}
+
+template <typename XT, int NT, int CW, int CPW, bool SA, int CTAS = 1>
+int launch_gemv_tma(const XT *x, const uint8_t *packed, const float *scales, float *y, int64_t m, int64_t n,
+                    int64_t k, int64_t kp, int g, int gshift, cudaStream_t st) {
+    using L = TmaGemvLayout<CW, CPW>;
+    size_t smem = 0;
+    int xstride = 0;
+    bool xs = false;
+    const int64_t tiles = cdiv(n, 16);
+    const int64_t grid = std::min<int64_t>(tiles, (int64_t)sm_count() * CTAS);
+    const int64_t max_pos = cdiv(tiles, grid) * cdiv(kp, L::kStageCols);
+    const int stages = tma_gemv_plan<CW, CPW>(m, k, kp, g, NT, (int)sizeof(XT), &smem, &xstride, &xs, CTAS, max_pos);
+    if (stages == 0) return invalid("TMA GEMV: shape does not fit in shared memory");
+    CUtensorMap wmap, smap;
+    int rc = make_tensor_map_2d(&wmap, packed, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)(kp / 2), (uint64_t)n,
+                                (uint64_t)(kp / 2), 128, 16, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != OQ_OK) return rc;
+    const int64_t groups = kp / g;
+    const bool stma = (groups * 4) % 16 == 0 && aligned(scales, 16) && (L::kStageCols / g) * 4 % 16 == 0;
+    if (stma) {
+        rc = make_tensor_map_2d(&smap, scales, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)groups, (uint64_t)n,
+                                (uint64_t)(groups * 4), (uint32_t)(L::kStageCols / g), 16,
+                                CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (rc != OQ_OK) return rc;
+    } else {
+        smap = wmap;  // unused
+    }
+    auto pick = [&](auto kern) -> int {
+        int rc2 = allow_max_smem(reinterpret_cast<const void *>(kern));
+        if (rc2 != OQ_OK) return rc2;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)grid);
+        cfg.blockDim = dim3((CW + 1) * 32);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        cudaError_t err = cudaLaunchKernelEx(&cfg, kern, wmap, smap, x, scales, y, (int)m, (int)n, (int)k, (int)kp,
+                                             gshift, xstride, stages);
+        if (err != cudaSuccess) {
+            set_error("int4_linear (TMA GEMV): launch failed: %s", cudaGetErrorString(err));
+            return OQ_ERR_CUDA;
+        }
+        return OQ_OK;
+    };
+    if (xs)
+        return stma ? pick(gemv_tma_kernel<XT, NT, CW, CPW, SA, true, true>)
+                    : pick(gemv_tma_kernel<XT, NT, CW, CPW, SA, true, false>);
+    return stma ? pick(gemv_tma_kernel<XT, NT, CW, CPW, SA, false, true>)
+                : pick(gemv_tma_kernel<XT, NT, CW, CPW, SA, false, false>);
+}
+
+// True when the TMA GEMV takes this shape (M <= 16, 32 <= g <= the stage
+// width, packed rows 16-byte aligned, and the shared-memory plan fits).
+template <int CW, int CPW, int CTAS = 1>
+bool tma_gemv_ok(int64_t m, int64_t k, int64_t kp, int g, const uint8_t *packed) {
+    size_t smem = 0;
+    int xstride = 0;
+    bool xs = false;
+    return m <= 16 && aligned(packed, 16) && (kp / 2) % 16 == 0 &&
+           tma_gemv_plan<CW, CPW>(m, k, kp, g, (int)((m + 7) / 8), 2, &smem, &xstride, &xs, CTAS) > 0;
+}
+
+// GEMV launch shapes, selected by the low bits of oq_int4_linear's
+// `config` (0 = automatic):
+//   1..7  register-ring kernel, (warps per CTA, chunks in flight per warp,
+//         CTAs per SM) = (8,4,2) (16,2,2) (12,2,2) (16,1,2) (8,2,3) (8,2,4)
+//         (8,4,4)
+//   8, 9  TMA-fed persistent kernel with 8 / 16 consumer warps, 32 KB
+//         stages (M <= 16)
+//   10    TMA-fed, 8 consumer warps, two CTAs per SM with the stage ring
+//         sized to the CTA's work, so consecutive launches overlap (PDL)
+// config & 16 (OQ_CONFIG_EXACT_ROUNDING) forces the exact weight rounding
+// for fp16 x, which otherwise uses the scale-after path when g % 128 == 0.
+constexpr int kGemvConfigs = 10;
+
+template <typename XT, int NT, bool SA>
+int launch_gemv_nt(int config, const XT *x, const uint8_t *packed, const float *scales, float *y, int64_t m,
+                   int64_t n, int64_t k, int64_t kp, int g, int gshift, cudaStream_t st) {
+    switch (config) {
+        case 1: return launch_gemv_t<XT, NT, 8, 4, 2, SA>(x, packed, scales, y, m, n, k, kp, gshift, st);
+        case 2: return launch_gemv_t<XT, NT, 16, 2, 2, SA>(x, packed, scales, y, m, n, k, kp, gshift, st);
+        case 3: return launch_gemv_t<XT, NT, 12, 2, 2, SA>(x, packed, scales, y, m, n, k, kp, gshift, st);
+        case 4: return launch_gemv_t<XT, NT, 16, 1, 2, SA>(x, packed, scales, y, m, n, k, kp, gshift, st);
+        case 6: return launch_gemv_t<XT, NT, 8, 2, 4, SA>(x, packed, scales, y, m, n, k, kp, gshift, st);
+        case 7: return launch_gemv_t<XT, NT, 8, 4, 4, SA>(x, packed, scales, y, m, n, k, kp, gshift, st);
+        case 8:
+            if constexpr (NT <= 2) return launch_gemv_tma<XT, NT, 8, 4, SA>(x, packed, scales, y, m, n, k, kp, g, gshift, st);
+            return invalid("TMA GEMV needs M <= 16");
+        case 9:
+            if constexpr (NT <= 2) return launch_gemv_tma<XT, NT, 16, 2, SA>(x, packed, scales, y, m, n, k, kp, g, gshift, st);
+            return invalid("TMA GEMV needs M <= 16");
+        case 10:
+            if constexpr (NT <= 2)
+                return launch_gemv_tma<XT, NT, 8, 4, SA, 2>(x, packed, scales, y, m, n, k, kp, g, gshift, st);
+            return invalid("TMA GEMV needs M <= 16");
+        default: return launch_gemv_t<XT, NT, 8, 2, 3, SA>(x, packed, scales, y, m, n, k, kp, gshift, st);
+    }
+}
+
+template <typename XT, bool SA>
+int launch_gemv_sa(int shape, const XT *x, const uint8_t *packed, const float *scales, float *y, int64_t m,
+                   int64_t n, int64_t k, int64_t kp, int g, int gshift, cudaStream_t st) {
+    switch ((m + 7) / 8) {
+        case 1: return launch_gemv_nt<XT, 1, SA>(shape, x, packed, scales, y, m, n, k, kp, g, gshift, st);
+        case 2: return launch_gemv_nt<XT, 2, SA>(shape, x, packed, scales, y, m, n, k, kp, g, gshift, st);
+        case 3: case 4: return launch_gemv_nt<XT, 4, SA>(shape, x, packed, scales, y, m, n, k, kp, g, gshift, st);
+        default: return launch_gemv_t<XT, 8, 8, 2, 1, SA>(x, packed, scales, y, m, n, k, kp, gshift, st);
+    }
 }
 
 template <typename XT>
 int launch_gemv(const XT *x, const uint8_t *packed, const float *scales, float *y, int64_t m, int64_t n, int64_t k,
-                int64_t kp, int g, cudaStream_t st) {
-    switch ((m + 7) / 8) {
-        case 1: return launch_gemv_t<XT, 1, 8, 4>(x, packed, scales, y, m, n, k, kp, g, st);
-        case 2: return launch_gemv_t<XT, 2, 8, 4>(x, packed, scales, y, m, n, k, kp, g, st);
-        case 3: case 4: return launch_gemv_t<XT, 4, 8, 2>(x, packed, scales, y, m, n, k, kp, g, st);
-        default: return launch_gemv_t<XT, 8, 8, 2>(x, packed, scales, y, m, n, k, kp, g, st);
+                int64_t kp, int g, int config, cudaStream_t st) {
+    int gshift = 0;
+    while ((1 << gshift) < g) ++gshift;
+    const int nt = (int)((m + 7) / 8);
+    int shape = config & 15;
+    const bool auto_shape = shape <= 0 || shape > kGemvConfigs;
+    if (auto_shape) {
+        if (nt == 1 && tma_gemv_ok<8, 4, 2>(m, k, kp, g, packed))
+            shape = 10;
+        else if (tma_gemv_ok<16, 2>(m, k, kp, g, packed))
+            shape = 9;
+        else if (tma_gemv_ok<8, 4>(m, k, kp, g, packed))
+            shape = 8;
+        else
+            shape = nt <= 2 ? 1 : 5;
     }
+    if ((shape == 8 && !tma_gemv_ok<8, 4>(m, k, kp, g, packed)) || (shape == 9 && !tma_gemv_ok<16, 2>(m, k, kp, g, packed)) ||
+        (shape == 10 && !tma_gemv_ok<8, 4, 2>(m, k, kp, g, packed)))
+        return invalid("TMA GEMV (config %d) does not take this shape", shape);
+    // Scale-after pays off for M <= 8; with two n-tiles its extra partial
+    // sums cost more registers than the exact path saves.
+    const bool exact = (config & OQ_CONFIG_EXACT_ROUNDING) != 0 || (auto_shape && nt > 1);
+    if constexpr (std::is_same<XT, __half>::value) {
+        if (!exact && g % 128 == 0)
+            return launch_gemv_sa<XT, true>(shape, x, packed, scales, y, m, n, k, kp, g, gshift, st);
+    }
+    return launch_gemv_sa<XT, false>(shape, x, packed, scales, y, m, n, k, kp, g, gshift, st);
 }
 
 template <typename XT>
@@ -345,8 +948,14 @@ int launch_simt(const XT *x, const uint8_t *packed, const float *scales, float *
 
 }  // namespace
 
-bool gemv_supported(int64_t m, int64_t k, int g, const void *x, const uint8_t *packed) {
-    return m >= 1 && m <= 64 && g % 32 == 0 && k % 8 == 0 && aligned(x, 16) && aligned(packed, 16);
+bool gemv_supported(int64_t m, int64_t n, int64_t k, int g, const void *x, const uint8_t *packed) {
+    if (!(m >= 1 && m <= 64 && g >= 32 && (g & (g - 1)) == 0 && k % 8 == 0 && aligned(x, 16) &&
+          aligned(packed, 16)))
+        return false;
+    const int64_t kp = cdiv(k, g) * g;
+    if (n >= (1ll << 31) || kp >= (1ll << 30) || n * (kp / 2) >= (1ll << 40)) return false;
+    // x from global memory needs KP == K and whole 128-column chunks.
+    return gemv_xs_bytes(m, kp, 2) > 0 || (kp == k && kp % 128 == 0);
 }
 
 }  // namespace oq
@@ -354,9 +963,8 @@ bool gemv_supported(int64_t m, int64_t k, int g, const void *x, const uint8_t *p
 using namespace oq;
 
 extern "C" int oq_int4_linear(const void *x, int x_dtype, const uint8_t *packed, const float *scales, float *y,
-                              int64_t m, int64_t n, int64_t k, int group_size, int kernel, int split_k,
+                              int64_t m, int64_t n, int64_t k, int group_size, int kernel, int config,
                               oq_stream_t stream) {
-    (void)split_k;
     clear_error();
     OQ_REQUIRE(x_dtype == OQ_F16 || x_dtype == OQ_BF16, "Input must be a 2D FP16 or BF16 tensor");
     OQ_REQUIRE(group_size >= 2 && group_size % 2 == 0, "Group size must be even and >= 2");
@@ -364,7 +972,7 @@ extern "C" int oq_int4_linear(const void *x, int x_dtype, const uint8_t *packed,
     OQ_REQUIRE(x && packed && scales && y, "null pointer argument");
     const int64_t kp = cdiv(k, group_size) * group_size;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    const bool gemv_ok = gemv_supported(m, k, group_size, x, packed);
+    const bool gemv_ok = gemv_supported(m, n, k, group_size, x, packed);
     int which = kernel;
     if (which == OQ_KERNEL_AUTO) {
         if (gemv_ok && m <= 64)
@@ -376,10 +984,12 @@ extern "C" int oq_int4_linear(const void *x, int x_dtype, const uint8_t *packed,
     }
     switch (which) {
         case OQ_KERNEL_GEMV:
-            OQ_REQUIRE(gemv_ok, "GEMV kernel needs M <= 64, group_size % 32 == 0, K % 8 == 0 and 16-byte aligned x/packed");
+            OQ_REQUIRE(gemv_ok, "GEMV kernel needs M <= 64, a power-of-two group_size >= 32, K % 8 == 0, 16-byte aligned x/packed, and x staged in shared memory or K a multiple of 128 and of the group");
             if (x_dtype == OQ_F16)
-                return launch_gemv(static_cast<const __half *>(x), packed, scales, y, m, n, k, kp, group_size, st);
-            return launch_gemv(static_cast<const __nv_bfloat16 *>(x), packed, scales, y, m, n, k, kp, group_size, st);
+                return launch_gemv(static_cast<const __half *>(x), packed, scales, y, m, n, k, kp, group_size, config,
+                                   st);
+            return launch_gemv(static_cast<const __nv_bfloat16 *>(x), packed, scales, y, m, n, k, kp, group_size,
+                               config, st);
         case OQ_KERNEL_TCGEN05:
             OQ_REQUIRE(gemm_tcgen05_supported(m, n, k, group_size, x, packed, y),
                        "tcgen05 kernel does not support this shape/alignment");

@@ -18,7 +18,7 @@ __all__ = ["int4_linear"]
 
 
 def int4_linear(x, packed, scales, out_features, group_size, *, block_m=64, block_n=64, block_k=64, num_warps=4,
-                kernel=None, out=None):
+                kernel=None, out=None, exact_rounding=False):
     """y = x @ W^T in fp32, W[n, k] = round_x(int4(n, k) * scales[n, k // g]).
 
     Arguments and errors follow triton_int4.py:78-118 (ValueError for each
@@ -32,6 +32,13 @@ def int4_linear(x, packed, scales, out_features, group_size, *, block_m=64, bloc
     (openquant_b200/tile_table.json) or `kernel` ("gemv", "simt",
     "tcgen05"); `out` may supply a preallocated fp32 (M, N) tensor.
     The launch is asynchronous on the current CUDA stream of x's device.
+
+    With fp16 x, M <= 8 and group_size % 128 == 0 the decode GEMV
+    multiplies x by the exact integer nibbles and applies each fp32 group
+    scale to the group's fp32 partial sum (closer to x.(q*s) than the
+    reference, and within the parity tolerance of it).  exact_rounding=True
+    instead rounds every weight to fp16 as the reference kernel does, bit
+    for bit; bf16 x and larger M always do.
     """
     if x.ndim != 2 or x.dtype not in (torch.float16, torch.bfloat16):
         raise ValueError("Input must be a 2D FP16 tensor")
@@ -77,6 +84,8 @@ def int4_linear(x, packed, scales, out_features, group_size, *, block_m=64, bloc
         if kernel not in nat.KERNELS:
             raise ValueError(f"unknown kernel {kernel!r}")
         sel, split = nat.KERNELS[kernel], 0
+    if exact_rounding:
+        split |= nat.CONFIG_EXACT_ROUNDING
     code = nat.OQ_F16 if x.dtype == torch.float16 else nat.OQ_BF16
     with torch.cuda.device(x.device):
         nat.check(nat.load().oq_int4_linear(nat.ptr(x), code, nat.ptr(packed), nat.ptr(scales), nat.ptr(out),

@@ -38,7 +38,18 @@ def make_case(m, n, k, g, dtype, seed=42, w_sigma=1.0):
     return x, q, xt
 
 
+def assert_no_device_error():
+    import ctypes
+
+    from openquant_b200 import _native as nat
+
+    code = ctypes.c_int32(-1)
+    nat.check(nat.load().oq_take_device_error(ctypes.byref(code)))
+    assert code.value == 0, f"kernel reported device error {code.value}"
+
+
 def check_against_oracle(y, x, q, g, dtype):
+    assert_no_device_error()
     name = "f16" if dtype == torch.float16 else "bf16"
     ref = orc.int4_linear(x, q.data, q.scales, q.shape[0], g, x_dtype=name)
     got = y.cpu().numpy()
@@ -63,10 +74,33 @@ def test_reference_test_shapes(shape, dtype):
     check_against_oracle(y, x, q, g, dtype)
 
 
+@pytest.mark.parametrize("cfg", [8, 9, 8 | 16, 9 | 16])
+@pytest.mark.parametrize("shape", [(1, 4096, 4096, 128), (1, 1000, 11008, 128), (16, 300, 4096, 64),
+                                   (9, 77, 1000, 32), (2, 4097, 1152, 256), (1, 16, 8, 32), (5, 40, 3000, 128)])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_tma_gemv_vs_oracle(shape, dtype, cfg):
+    """The TMA-fed persistent GEMV (configs 8 / 9; | 16 = exact rounding)."""
+    import ctypes
+
+    from openquant_b200 import _native as nat
+
+    m, n, k, g = shape
+    if g > 32 * (8 if (cfg & 15) == 8 else 16):
+        pytest.skip("group too large for this config")
+    x, q, xt = make_case(m, n, k, g, dtype, seed=m + n + k, w_sigma=0.02)
+    p, s = torch.from_numpy(q.data).cuda(), torch.from_numpy(q.scales).cuda()
+    y = torch.empty(m, n, device="cuda")
+    code = nat.OQ_F16 if dtype == torch.float16 else nat.OQ_BF16
+    st = nat.load().oq_int4_linear(nat.ptr(xt), code, nat.ptr(p), nat.ptr(s), nat.ptr(y), m, n, k, g, 1, cfg,
+                                   nat.stream_of(xt.device))
+    nat.check(st)
+    check_against_oracle(y, x, q, g, dtype)
+
+
 GEMV_SHAPES = [
     (1, 16, 32, 32), (1, 17, 64, 32), (2, 48, 96, 32), (4, 100, 200, 64), (8, 33, 256, 128), (9, 64, 1024, 128),
     (16, 4096, 4096, 128), (1, 4096, 4096, 128), (5, 31, 160, 32), (16, 8, 8, 32), (1, 1, 8, 32), (64, 70, 384, 128),
-    (40, 130, 520, 64), (1, 1000, 11008, 128),
+    (40, 130, 520, 64), (1, 1000, 11008, 128), (16, 256, 11008, 128), (48, 64, 2048, 64), (3, 40, 200, 32),
 ]
 
 
@@ -174,5 +208,31 @@ def test_weight_rounding_is_bit_exact(shape, dtype, kernel):
         cols = np.arange(start, min(k, start + m))
         x = np.zeros((len(cols), k), np.float32)
         x[np.arange(len(cols)), cols] = 1.0
-        y = int4_linear(torch.from_numpy(x).cuda().to(dtype), p, s, n, g, kernel=kernel)
+        y = int4_linear(torch.from_numpy(x).cuda().to(dtype), p, s, n, g, kernel=kernel, exact_rounding=True)
         assert_float_bits_equal(y.cpu().numpy(), wref[:, cols].T.copy(), f"cols {start}")
+
+
+@pytest.mark.parametrize("shape", [(1, 4096, 4096), (4, 4096, 22016), (16, 11008, 4096), (3, 1024, 512), (64, 256, 1024)])
+def test_fp16_scale_after_vs_exact_rounding(shape):
+    """fp16 GEMV default (exact integer nibbles, fp32 group scale applied to
+    the group's partial sum) vs the reference's per-weight fp16 rounding:
+    both within the parity tolerance of the oracle, and the default is the
+    closer of the two to the unrounded product x.(q*s)."""
+    from openquant.groupwise import quantize_int4_groupwise
+    from openquant.triton_int4 import int4_linear
+
+    m, k, n = shape
+    gen = torch.Generator(device="cuda").manual_seed(m + k + n)
+    w = torch.randn(n, k, device="cuda", generator=gen).mul_(0.02)
+    q = quantize_int4_groupwise(w, 128)
+    x = torch.randn(m, k, device="cuda", generator=gen).half()
+    wd = orc.dequantize_int4_groupwise(q.data.cpu().numpy(), q.scales.cpu().numpy(), (n, k), 128)
+    ref = x.double() @ torch.from_numpy(orc.round_to_dtype(wd, "f16")).cuda().double().T
+    true = x.double() @ torch.from_numpy(wd).cuda().double().T
+    fast = int4_linear(x, q.data, q.scales, n, 128).double()
+    exact = int4_linear(x, q.data, q.scales, n, 128, exact_rounding=True).double()
+    for y in (fast, exact):
+        assert ((y - ref).norm() / ref.norm()).item() <= REL_L2
+        assert (y - ref).abs().max().item() <= MAX_ABS
+    assert ((exact - ref).norm() / ref.norm()).item() < 1e-5
+    assert (fast - true).norm().item() < (exact - true).norm().item()
