@@ -1,16 +1,305 @@
-// Prefill-side (M >= 64) dequant-GEMM on the tcgen05 tensor cores.
-#include "oq_common.cuh"
+// Prefill-side fused INT4 dequant + GEMM on the 5th-generation tensor cores
+// (tcgen05 / TMEM), sm_100a.
+//
+// y[M][N] = x[M][K] . W^T with W[n][k] = round_x(fl32(q * s)) exactly as the
+// reference kernel rounds its weights (openquant/triton_int4.py:62-65), fp32
+// accumulation.  The product is computed transposed, D = W . x^T, so that the
+// dequantized weights can be the MMA's A operand held in tensor memory:
+//
+//   tile      : 128 weight rows (MMA M = TMEM lanes) x 256 batch rows (MMA N)
+//   k-block   : 64 columns (one 128-byte swizzle atom of 16-bit x)
+//   producer  : warp 0 -- TMA of the x tile (256 x 64, 128-byte swizzle) and
+//               of the packed weight tile (128 rows x 32 bytes) per k-block
+//               into a 4-stage shared-memory ring (full[s])
+//   dequant   : warps 4..7 -- thread r owns weight row r of the tile: it
+//               reads its 32 packed bytes, forms 64 exactly-rounded 16-bit
+//               weights and writes them straight into the stage's TMEM A slot
+//               with tcgen05.st (no shared-memory round trip), then signals
+//               deq[s]
+//   MMA       : warp 1, one thread -- four tcgen05.mma (K = 16 each) per
+//               k-block, A from TMEM, B (x) from shared memory by descriptor,
+//               D (128 x 256 fp32) accumulating in TMEM; tcgen05.commit frees
+//               the stage (empty[s]) and, after the last k-block, publishes
+//               the tile (acc_full)
+//   epilogue  : warps 8..11 -- tcgen05.ld of the accumulator, fp32 stores
+//               (each warp store is 32 consecutive weight rows of one batch
+//               row: 128 coalesced bytes), then acc_empty
+//   warp 2    : TMEM allocation / release (512 columns: accumulator 256 +
+//               4 A slots of 32)
+//
+// The grid is persistent (one CTA per SM); tiles are ordered so that the
+// CTAs working on one weight tile run together, so each packed weight tile
+// is read from HBM once while x stays resident in L2.  Every mbarrier wait
+// is bounded (oq_sm100.cuh); on a timeout the roles drain what they have in
+// flight and the kernel returns with the device error word set.
+#include "oq_dequant.cuh"
+#include "oq_sm100.cuh"
+
+#include <mutex>
+#include <set>
 
 namespace oq {
+namespace {
 
-int gemm_tcgen05_supported(int64_t, int64_t, int64_t, int, const void *, const uint8_t *, const float *) {
-    return 0;
+constexpr int kBN = 128;                 // weight rows per tile (MMA M, TMEM lanes)
+constexpr int kBX = 256;                 // batch rows per tile (MMA N)
+constexpr int kBK = 64;                  // columns per k-block
+constexpr int kStages = 4;
+constexpr int kXBytes = kBX * kBK * 2;   // 32 KB x tile per stage
+constexpr int kWBytes = kBN * kBK / 2;   // 4 KB packed tile per stage
+constexpr int kAccCols = kBX;            // fp32 accumulator columns
+constexpr int kACols = kBK / 2;          // TMEM columns of one A slot (two 16-bit values per column)
+constexpr int kTmemCols = 512;
+constexpr int kThreads = 384;            // 12 warps
+constexpr size_t kSmemBytes = 1024 + (size_t)kStages * (kXBytes + kWBytes) + 256;
+
+static_assert(kAccCols + kStages * kACols <= kTmemCols, "TMEM budget");
+
+template <typename XT>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_int4_tcgen05_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
+                             const float *__restrict__ scales, float *__restrict__ y, int m, int n, int kp, int g) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+    uint8_t *xbuf = smem;                                    // [S][256 rows][128 B], swizzled
+    uint8_t *wbuf = xbuf + (size_t)kStages * kXBytes;        // [S][128 rows][32 B]
+    uint64_t *full = reinterpret_cast<uint64_t *>(wbuf + (size_t)kStages * kWBytes);
+    uint64_t *deq = full + kStages;
+    uint64_t *empty = deq + kStages;
+    uint64_t *acc_full = empty + kStages;
+    uint64_t *acc_empty = acc_full + 1;
+    uint64_t *mma_done = acc_empty + 1;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mma_done + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tiles_n = (n + kBN - 1) / kBN, tiles_m = (m + kBX - 1) / kBX;
+    const int tiles = tiles_n * tiles_m;
+    const int kblocks = (kp + kBK - 1) / kBK;
+    const int groups = kp / g;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], 1);   // producer's expect_tx arrival
+            mbar_init(&deq[s], 4);    // one arrival per dequant warp
+            mbar_init(&empty[s], 1);  // tcgen05.commit
+        }
+        mbar_init(acc_full, 1);
+        mbar_init(acc_empty, 4);
+        mbar_init(mma_done, 1);
+        fence_barrier_init();
+    }
+    if (warp == 2) {
+        tmem_alloc(tmem_slot, kTmemCols);
+        tmem_relinquish();
+        tc_fence_before();
+    }
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;");
+
+    if (warp == 0) {
+        // ------------------------------------------------------ producer
+        if (lane == 0) {
+            tma_prefetch_desc(&xmap);
+            tma_prefetch_desc(&wmap);
+            int it = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+                const int n0 = (tile / tiles_m) * kBN, m0 = (tile % tiles_m) * kBX;
+                for (int kb = 0; kb < kblocks; ++kb, ++it) {
+                    const int s = it % kStages, r = it / kStages;
+                    if (r > 0 && !(ok = mbar_wait(&empty[s], (r - 1) & 1))) break;
+                    mbar_arrive_expect_tx(&full[s], kXBytes + kWBytes);
+                    tma_load_2d(xbuf + (size_t)s * kXBytes, &xmap, &full[s], kb * kBK, m0);
+                    tma_load_2d(wbuf + (size_t)s * kWBytes, &wmap, &full[s], kb * (kBK / 2), n0);
+                }
+            }
+            // Drain: every issued stage's copies must land before the CTA
+            // exits (normally the consumers have waited for all of them).
+            for (int j = (it > kStages ? it - kStages : 0); j < it; ++j)
+                mbar_wait(&full[j % kStages], (j / kStages) & 1);
+        }
+    } else if (warp == 1) {
+        // ----------------------------------------------------------- MMA
+        if (lane == 0) {
+            constexpr uint32_t idesc = umma_idesc_f16(kBN, kBX, std::is_same<XT, __nv_bfloat16>::value);
+            int it = 0, ti = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++ti) {
+                if (ti > 0 && !(ok = mbar_wait(acc_empty, (ti - 1) & 1))) break;
+                tc_fence_after();
+                for (int kb = 0; kb < kblocks; ++kb, ++it) {
+                    const int s = it % kStages, r = it / kStages;
+                    if (!(ok = mbar_wait(&full[s], r & 1))) break;
+                    if (!(ok = mbar_wait(&deq[s], r & 1))) break;
+                    tc_fence_after();
+                    const uint64_t bdesc = umma_desc_sw128(smem_u32(xbuf + (size_t)s * kXBytes));
+                    const uint32_t a_tmem = tmem + kAccCols + s * kACols;
+#pragma unroll
+                    for (int kk = 0; kk < kBK / 16; ++kk)
+                        tc_mma_ts(tmem, a_tmem + kk * 8, bdesc + (uint64_t)(kk * 32 / 16), idesc,
+                                  (kb | kk) != 0 ? 1u : 0u);
+                    tc_commit(&empty[s]);
+                }
+                if (ok) tc_commit(acc_full);
+            }
+            // Every MMA this thread issued has completed once mma_done fires.
+            tc_commit(mma_done);
+            mbar_wait(mma_done, 0);
+        }
+    } else if (warp >= 4 && warp < 8) {
+        // ------------------------------------------------------- dequant
+        const int q = warp - 4;         // TMEM lane quarter
+        const int r = q * 32 + lane;    // weight row within the tile
+        int it = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+            const int n0 = (tile / tiles_m) * kBN;
+            const float *srow = scales + (size_t)min(n0 + r, n - 1) * groups;
+            for (int kb = 0; kb < kblocks; ++kb, ++it) {
+                const int s = it % kStages, rd = it / kStages;
+                const int c0 = kb * kBK;
+                const float s0 = __ldg(srow + min(c0 / g, groups - 1));
+                const float s1 = __ldg(srow + min((c0 + 32) / g, groups - 1));
+                // Warp-uniform outcome: tcgen05.st below is .sync.aligned.
+                ok = __all_sync(0xffffffffu, mbar_wait(&full[s], rd & 1));
+                if (!ok) break;
+                const uint4 w0 = *reinterpret_cast<const uint4 *>(wbuf + (size_t)s * kWBytes + r * 32);
+                const uint4 w1 = *reinterpret_cast<const uint4 *>(wbuf + (size_t)s * kWBytes + r * 32 + 16);
+                const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+                const DqScale d0 = make_dq_scale(s0), d1 = make_dq_scale(s1);
+                uint32_t a[32];
+                auto run = [&](auto fast_tag) {
+                    constexpr bool FAST = decltype(fast_tag)::value;
+#pragma unroll
+                    for (int wd = 0; wd < 8; ++wd) {
+                        uint32_t h0[2], h1[2];
+                        dq_half<XT, 0, FAST>(words[wd], wd < 4 ? d0 : d1, h0);
+                        dq_half<XT, 1, FAST>(words[wd], wd < 4 ? d0 : d1, h1);
+                        a[4 * wd + 0] = h0[0];
+                        a[4 * wd + 1] = h0[1];
+                        a[4 * wd + 2] = h1[0];
+                        a[4 * wd + 3] = h1[1];
+                    }
+                };
+                if (__all_sync(0xffffffffu, d0.fast && d1.fast))
+                    run(std::true_type{});
+                else
+                    run(std::false_type{});
+                tmem_st_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + kAccCols + s * kACols, a);
+                tc_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&deq[s]);
+            }
+        }
+    } else if (warp >= 8) {
+        // ------------------------------------------------------ epilogue
+        const int q = warp - 8;
+        int ti = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++ti) {
+            const int n0 = (tile / tiles_m) * kBN, m0 = (tile % tiles_m) * kBX;
+            ok = __all_sync(0xffffffffu, mbar_wait(acc_full, ti & 1));  // tcgen05.ld is .sync.aligned
+            if (!ok) break;
+            tc_fence_after();
+            const int row = n0 + q * 32 + lane;
+#pragma unroll 1
+            for (int c = 0; c < kAccCols / 32; ++c) {
+                uint32_t v[32];
+                tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + c * 32, v);
+                tc_wait_ld();
+                if (row < n) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const int mb = m0 + c * 32 + j;
+                        if (mb < m) y[(size_t)mb * n + row] = __uint_as_float(v[j]);
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acc_empty);
+        }
+    }
+
+    __syncthreads();
+    if (warp == 2) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
 }
 
-int gemm_tcgen05_launch(const void *, int, const uint8_t *, const float *, float *, int64_t, int64_t, int64_t, int,
-                        cudaStream_t) {
-    set_error("tcgen05 GEMM not available");
-    return OQ_ERR_UNSUPPORTED;
+int allow_smem(const void *kern, size_t bytes) {
+    static std::mutex mu;
+    static std::set<std::pair<const void *, int>> done;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (done.count({kern, dev})) return OQ_OK;
+    OQ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+    done.insert({kern, dev});
+    return OQ_OK;
+}
+
+template <typename XT>
+int launch(const XT *x, CUtensorMapDataType xtype, const uint8_t *packed, const float *scales, float *y, int64_t m,
+           int64_t n, int64_t k, int g, cudaStream_t st) {
+    const int64_t kp = cdiv(k, g) * g;
+    CUtensorMap xmap, wmap;
+    int rc = make_tensor_map_2d(&xmap, x, xtype, 2, (uint64_t)k, (uint64_t)m, (uint64_t)(k * 2), kBK, kBX,
+                                CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != OQ_OK) return rc;
+    rc = make_tensor_map_2d(&wmap, packed, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)(kp / 2), (uint64_t)n,
+                            (uint64_t)(kp / 2), kBK / 2, kBN, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc != OQ_OK) return rc;
+    auto kern = gemm_int4_tcgen05_kernel<XT>;
+    rc = allow_smem(reinterpret_cast<const void *>(kern), kSmemBytes);
+    if (rc != OQ_OK) return rc;
+    const int64_t tiles = cdiv(n, kBN) * cdiv(m, kBX);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)std::min<int64_t>(tiles, sm_count()));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t err = cudaLaunchKernelEx(&cfg, kern, xmap, wmap, scales, y, (int)m, (int)n, (int)kp, g);
+    if (err != cudaSuccess) {
+        set_error("int4_linear (tcgen05 GEMM): launch failed: %s", cudaGetErrorString(err));
+        return OQ_ERR_CUDA;
+    }
+    return OQ_OK;
+}
+
+}  // namespace
+
+// The tcgen05 GEMM takes: K % 8 == 0 (16-byte x rows for TMA), a group size
+// that is a multiple of 32 (each 32-column half of a k-block has one scale)
+// with KP % 32 == 0, 16-byte aligned x and packed, and sizes below 2^31.
+int gemm_tcgen05_supported(int64_t m, int64_t n, int64_t k, int g, const void *x, const uint8_t *packed,
+                           const float *y) {
+    (void)y;
+    if (m < 1 || n < 1 || k < 1 || g < 32 || g % 32 != 0) return 0;
+    const int64_t kp = cdiv(k, g) * g;
+    if (k % 8 != 0 || kp % 32 != 0) return 0;
+    if (!aligned(x, 16) || !aligned(packed, 16)) return 0;
+    if (m >= (1ll << 31) || n >= (1ll << 31) || kp >= (1ll << 31) || m * n >= (1ll << 40)) return 0;
+    return 1;
+}
+
+int gemm_tcgen05_launch(const void *x, int x_dtype, const uint8_t *packed, const float *scales, float *y, int64_t m,
+                        int64_t n, int64_t k, int g, cudaStream_t st) {
+    if (x_dtype == OQ_BF16)
+        return launch(static_cast<const __nv_bfloat16 *>(x), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, packed, scales, y, m,
+                      n, k, g, st);
+    return launch(static_cast<const __half *>(x), CU_TENSOR_MAP_DATA_TYPE_FLOAT16, packed, scales, y, m, n, k, g, st);
 }
 
 }  // namespace oq

@@ -101,7 +101,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
 // ------------------------------------------------------------------ TMA --
 
 // 2-D tiled TMA load of a box at element coordinates (c0 innermost, c1)
-// into shared memory, completing `bytes` on the mbarrier.  No multicast.
+// into shared memory of this CTA only, completing its bytes on the mbarrier.
 __device__ __forceinline__ void tma_load_2d(void *smem_dst, const CUtensorMap *map, uint64_t *bar, int c0, int c1) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"

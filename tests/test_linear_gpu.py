@@ -184,7 +184,50 @@ def test_deterministic_repeat():
     assert torch.equal(a, b)
 
 
-@pytest.mark.parametrize("kernel", ["gemv", "simt", None])
+PREFILL_SHAPES = [
+    (64, 128, 64, 32), (100, 200, 136, 64), (256, 256, 1024, 128), (300, 129, 520, 32), (17, 1000, 4096, 128),
+    (512, 1024, 2048, 128), (513, 384, 8192, 128), (1024, 128, 200, 64),
+]
+
+
+@pytest.mark.parametrize("shape", PREFILL_SHAPES)
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_prefill_tcgen05_vs_oracle(shape, dtype):
+    """The tcgen05/TMEM GEMM against the oracle (ragged M, N, K; g 32..128)."""
+    from openquant.triton_int4 import int4_linear
+
+    m, n, k, g = shape
+    x, q, xt = make_case(m, n, k, g, dtype, seed=m + 3 * n + k, w_sigma=0.02)
+    y = int4_linear(xt, torch.from_numpy(q.data).cuda(), torch.from_numpy(q.scales).cuda(), n, g, kernel="tcgen05")
+    check_against_oracle(y, x, q, g, dtype)
+
+
+def test_prefill_tcgen05_llama70b_shape_sampled():
+    """M = 2048, (K, N) = (8192, 28672) at bf16: compare sampled outputs with
+    an fp64 product of the exactly-rounded weights."""
+    from openquant.groupwise import quantize_int4_groupwise
+    from openquant.triton_int4 import int4_linear
+
+    m, k, n, g = 2048, 8192, 28672, 128
+    gen = torch.Generator(device="cuda").manual_seed(7)
+    w = torch.randn(n, k, device="cuda", generator=gen).mul_(0.02).to(torch.bfloat16)
+    q = quantize_int4_groupwise(w, g)
+    del w
+    x = torch.randn(m, k, device="cuda", generator=gen).to(torch.bfloat16)
+    y = int4_linear(x, q.data, q.scales, n, g)
+    assert_no_device_error()
+    rows = torch.arange(0, n, 97, device="cuda")
+    packed = q.data.view(n, k // 2)[rows].cpu().numpy().reshape(-1)
+    sc = q.scales[rows].cpu().numpy()
+    wr = orc.round_to_dtype(orc.dequantize_int4_groupwise(packed, sc, (len(rows), k), g), "bf16")
+    ref = x.double() @ torch.from_numpy(wr).cuda().double().T
+    got = y[:, rows].double()
+    err = got - ref
+    assert (err.norm() / ref.norm()).item() <= REL_L2
+    assert err.abs().max().item() <= MAX_ABS
+
+
+@pytest.mark.parametrize("kernel", ["gemv", "simt", "tcgen05", None])
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("shape", [(48, 512, 128), (33, 256, 64), (40, 96, 32)])
 def test_weight_rounding_is_bit_exact(shape, dtype, kernel):
@@ -196,7 +239,7 @@ def test_weight_rounding_is_bit_exact(shape, dtype, kernel):
     from conftest import assert_float_bits_equal
 
     n, k, g = shape
-    m = 64 if kernel != "simt" else 16
+    m = {"simt": 16, "tcgen05": 256}.get(kernel, 64)
     rng = np.random.default_rng(n + k + g)
     w = rng.normal(0, 0.05, (n, k)).astype(np.float32)
     w[:, ::7] *= 1e-3  # small groups exercise other exponents
