@@ -246,6 +246,84 @@ def run_reference(args):
 # ---------------------------------------------------------- GPU side --
 
 
+def measure_gemm(dev, peaks, steps=10, warmup=3):
+    """TFLOP/s of the prefill GEMM at M = 2048, (K, N) = (8192, 28672) (the
+    Llama-3-70B gate/up projection), bf16 x, group 128, two weight copies
+    (2 x 117 MB packed, beyond L2) alternated; CUDA-graph replay, CUDA events."""
+    import ctypes
+
+    import torch
+
+    from openquant_b200 import _native as nat
+    from openquant_b200.groupwise import quantize_int4_groupwise
+
+    lib = nat.load()
+    m, k, n, g = 2048, 8192, 28672, 128
+    gen = torch.Generator(device=dev).manual_seed(77)
+    w = torch.randn(n, k, generator=gen, device=dev).mul_(0.02).to(torch.bfloat16)
+    q = quantize_int4_groupwise(w, g)
+    del w
+    packs, scs = [q.data, q.data.clone()], [q.scales, q.scales.clone()]
+    x = torch.randn(m, k, generator=gen, device=dev).to(torch.bfloat16)
+    y = torch.empty(m, n, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+
+    def launch(count, h):
+        for i in range(count):
+            st = lib.oq_int4_linear(ctypes.c_void_p(x.data_ptr()), nat.OQ_BF16, ctypes.c_void_p(packs[i % 2].data_ptr()),
+                                    ctypes.c_void_p(scs[i % 2].data_ptr()), ctypes.c_void_p(y.data_ptr()), m, n, k, g,
+                                    0, 0, h)
+            if st != 0:
+                raise RuntimeError(nat.last_error())
+
+    with torch.cuda.stream(stream):
+        launch(warmup, ctypes.c_void_p(stream.cuda_stream))
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        launch(steps, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    graph.replay()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        graph.replay()
+        end.record(stream)
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end) / steps
+    tflops = 2.0 * m * n * k / (ms / 1e3) / 1e12
+    # spot check against the exactly-rounded weights on sampled columns
+    from oq_oracle import dequantize_int4_groupwise as deq, round_to_dtype
+
+    rows = torch.arange(0, n, 1021, device=dev)
+    wr = round_to_dtype(deq(q.data.view(n, k // 2)[rows].cpu().numpy().reshape(-1), q.scales[rows].cpu().numpy(),
+                            (len(rows), k), g), "bf16")
+    ref = x.double() @ torch.from_numpy(wr).to(dev).double().T
+    rel = ((y[:, rows].double() - ref).norm() / ref.norm()).item()
+    assert rel < 1e-3, rel
+    del graph
+    return {
+        "metric": "INT4 dequant-GEMM TFLOP/s at M=2048",
+        "workload": "int4_gemm_m2048_k8192_n28672_g128_bf16",
+        "value": tflops,
+        "unit": "TFLOP/s",
+        "ms_per_step": ms,
+        "steps": steps,
+        "roofline": {
+            "bound": "tensor",
+            "achieved": tflops,
+            "peak": peaks["bf16_tflops"],
+            "unit": "TFLOP/s",
+            "frac": tflops / peaks["bf16_tflops"],
+            "frac_of_sustained": tflops / peaks["bf16_tflops_sustained"],
+            "traffic": read_traffic("gemm_m2048_k8192_n28672_g128"),
+            "algorithmic_flops_per_launch": 2 * m * n * k,
+        },
+        "gpu_launches": steps,
+        "check_rel_l2": rel,
+    }
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -425,6 +503,9 @@ def run_ours(args):
         "clocks": clk,
         "check_rel_l2": rel,
     }
+    if world == 1 and not args.no_gemm:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        line["also"] = [measure_gemm(dev, peaks)]
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline()
     del g_chunk, g_rest
@@ -443,6 +524,7 @@ def main(argv=None):
     ap.add_argument("--warmup", type=int, default=20000)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-gemm", action="store_true", help="skip the M=2048 prefill GEMM measurement")
     args = ap.parse_args(argv)
     if args.steps < 1 or args.warmup < 0:
         ap.error("steps must be >= 1 and warmup >= 0")
