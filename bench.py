@@ -162,9 +162,13 @@ def cpu_gemv_sample(rows, threads):
         wd = orc.dequantize_int4_groupwise(data2[r0:r1].reshape(-1), scales[r0:r1], (r1 - r0, K), G)
         return x @ orc.round_to_dtype(wd, "f16").T
 
-    t0 = time.perf_counter()
-    y = np.concatenate(orc.threaded_rows(block, rows, threads=threads, min_rows=16), axis=1)
-    dt = time.perf_counter() - t0
+    from threadpoolctl import threadpool_limits
+
+    # One BLAS thread per worker thread: the row blocks already use every core.
+    with threadpool_limits(limits=1):
+        t0 = time.perf_counter()
+        y = np.concatenate(orc.threaded_rows(block, rows, threads=threads, min_rows=16), axis=1)
+        dt = time.perf_counter() - t0
     assert y.shape == (M, rows)
     sample_bytes = rows * KP // 2 + rows * (KP // G) * 4 + M * K * 2 + M * rows * 4
     return dt, sample_bytes
@@ -192,7 +196,7 @@ def cpu_baseline(budget_s=10.0):
         "cores": threads,
         "kind": "port",
         "sample": f"{len(times)} full {N}x{K} g={G} layers (dequantize + fp16 round + x@W^T, NumPy/OpenBLAS, "
-                  f"{threads} threads), median {med * 1e3:.1f} ms",
+                  f"{threads} threads over row blocks, 1 BLAS thread each), median {med * 1e3:.1f} ms",
     }
 
 

@@ -1,0 +1,136 @@
+"""`openquant tune`: offline kernel / launch-shape search for int4_linear.
+
+The reference searches Triton block shapes on one problem
+(openquant/autotune.py:14-195: every config is checked against
+x16 @ restored16.T with assert_close(rtol=atol=0.02), timed as the median of
+30 calls, the fastest reported).  Here every candidate is a hand-written
+sm_100a kernel and launch shape of oq_int4_linear -- the TMA-fed and
+register-ring GEMVs, the tcgen05 GEMM and the CUDA-core kernel -- checked the
+same way, timed the same way, and the winner per (M bucket, N, K, g) is
+written to openquant_b200/tile_table.json, which int4_linear reads.
+"""
+import argparse
+import json
+from statistics import median
+
+import torch
+
+from . import _native as nat
+from . import tile_table
+from .group_benchmark import restore_groupwise_torch
+from .groupwise import quantize_int4_groupwise
+
+__all__ = ["CONFIGS", "SHAPES", "candidates", "time_gpu", "tune_shape", "main"]
+
+# The reference's Triton (BM, BN, BK, warps) list (openquant/autotune.py:14-25).
+# int4_linear still accepts these keywords; they select nothing here.
+CONFIGS = [
+    (16, 32, 32, 4), (16, 64, 64, 4), (32, 32, 64, 4), (32, 64, 64, 4), (32, 64, 128, 4),
+    (32, 128, 64, 4), (64, 64, 64, 4), (64, 64, 128, 4), (64, 128, 64, 8), (64, 128, 128, 8),
+]
+
+# (M, K, N, g, x dtype): the reference's tuning problem, the Llama-2-7B decode
+# layer set at M in {1, 4, 16} and the Llama-3-70B MLP prefill shapes.
+SHAPES = [(128, 2048, 2048, 32, torch.float16)]
+SHAPES += [(m, k, n, 128, torch.float16) for m in (1, 4, 16)
+           for k, n in ((4096, 12288), (4096, 4096), (4096, 22016), (11008, 4096))]
+SHAPES += [(m, k, n, 128, torch.bfloat16) for m in (512, 2048) for k, n in ((8192, 28672), (28672, 8192))]
+
+
+def candidates(m):
+    """(name, kernel code, config) pairs worth trying at batch size m."""
+    out = []
+    if m <= 64:
+        shapes = range(1, 11) if m <= 16 else range(1, 8)
+        out += [(f"gemv:{c}", nat.KERNELS["gemv"], c) for c in shapes]
+    out.append(("tcgen05", nat.KERNELS["tcgen05"], 0))
+    if m <= 256:
+        out.append(("simt", nat.KERNELS["simt"], 0))
+    return out
+
+
+def time_gpu(fn, repetitions=30):
+    """Median CUDA-event time in ms after 10 warm-up calls (autotune.py:28-49)."""
+    with torch.inference_mode():
+        for _ in range(10):
+            fn()
+        torch.cuda.synchronize()
+        times = []
+        for _ in range(repetitions):
+            start = torch.cuda.Event(enable_timing=True)
+            end = torch.cuda.Event(enable_timing=True)
+            start.record()
+            fn()
+            end.record()
+            end.synchronize()
+            times.append(start.elapsed_time(end))
+    return median(times)
+
+
+def tune_shape(m, k, n, g, dtype, seed=0, verbose=True):
+    """Returns (best name, kernel, config, ms) and prints every candidate."""
+    gen = torch.Generator(device="cuda").manual_seed(seed)
+    w = torch.randn(n, k, device="cuda", generator=gen).mul_(0.02)
+    q = quantize_int4_groupwise(w, g)
+    x = torch.randn(m, k, device="cuda", generator=gen).to(dtype)
+    with torch.inference_mode():
+        wr = restore_groupwise_torch(q.data, q.scales, (n, k), g).to(dtype)
+        reference = (x.float() @ wr.float().T)
+    y = torch.empty(m, n, device="cuda")
+    code = nat.OQ_F16 if dtype == torch.float16 else nat.OQ_BF16
+    lib = nat.load()
+    results, failures = [], []
+    for name, kern, cfg in candidates(m):
+        def run():
+            nat.check(lib.oq_int4_linear(nat.ptr(x), code, nat.ptr(q.data), nat.ptr(q.scales), nat.ptr(y), m, n, k,
+                                         g, kern, cfg, nat.stream_of(x.device)))
+            return y
+
+        try:
+            torch.testing.assert_close(run(), reference, rtol=0.02, atol=0.02)
+            results.append((time_gpu(run), name, kern, cfg))
+        except (ValueError, RuntimeError, AssertionError) as exc:
+            failures.append((name, str(exc).splitlines()[0][:120]))
+    results.sort()
+    if verbose:
+        dt = "fp16" if dtype == torch.float16 else "bf16"
+        print(f"\n(M={m}, K={k}, N={n}, g={g}, {dt})")
+        for ms, name, _, _ in results:
+            print(f"  {name:<10} {ms * 1e3:>10.1f} us")
+        for name, why in failures:
+            print(f"  {name:<10} {'-':>10}    not taken: {why}")
+    if not results:
+        return None
+    ms, name, kern, cfg = results[0]
+    return name, kern, cfg, ms
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(prog="openquant tune", description=__doc__)
+    ap.add_argument("--output", default=tile_table.TABLE_PATH, help="tile table to write")
+    ap.add_argument("--quick", action="store_true", help="only the reference's tuning problem")
+    args = ap.parse_args(argv)
+    if not torch.cuda.is_available():
+        raise RuntimeError("CUDA unavailable")
+    nat.require_device()
+    print("\nOPENQUANT-B200 - KERNEL TUNING")
+    print("GPU:", torch.cuda.get_device_name(0))
+    entries = []
+    for (m, k, n, g, dtype) in (SHAPES[:1] if args.quick else SHAPES):
+        best = tune_shape(m, k, n, g, dtype)
+        if best is None:
+            continue
+        name, kern, cfg, ms = best
+        print(f"  -> fastest verified: {name} ({ms * 1e3:.1f} us)")
+        entries.append({"key": [tile_table.m_bucket(m), n, k, g], "kernel": kern, "split_k": cfg,
+                        "name": name, "us": round(ms * 1e3, 2), "dtype": str(dtype).replace("torch.", "")})
+    with open(args.output, "w") as f:
+        json.dump({"device": torch.cuda.get_device_name(0), "entries": entries}, f, indent=1)
+        f.write("\n")
+    tile_table.reset()
+    print(f"\nwrote {len(entries)} entries to {args.output}")
+    return 0
+
+
+if __name__ == "__main__":
+    main()
