@@ -115,3 +115,7 @@ def stream_of(device):
     import torch
 
     return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def ptr_of_stream(stream):
+    return ctypes.c_void_p(stream.cuda_stream)

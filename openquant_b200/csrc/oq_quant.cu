@@ -31,6 +31,36 @@ __device__ __forceinline__ float block_max(float v, float *smem) {
     return r;
 }
 
+// Eight quotients q_i = clip(rint(fl(v_i / s)), -qmax, qmax) as the bit
+// patterns of (q_i + 1.5*2^23) (low byte / nibble = q_i), like quant_bits but
+// with packed f32x2 arithmetic: r = v * (1/s), t = r + 1.5*2^23 (round half
+// to even), d = r - (t - 1.5*2^23).  When any lane of `mask` has a quotient
+// within 1e-3 of a tie (|d| >= 0.499) or a scale that is not a normal float
+// (zero-substituted, subnormal, NaN), those lanes redo all eight with
+// quant_bits (IEEE quotient, clipping, NaN -> 0).  For a normal scale derived
+// from the values' max, |v/s| <= qmax up to a few ulps, so no clip is needed.
+__device__ __forceinline__ void quant8(const float (&v)[8], float s, float inv, float qmax, uint32_t (&bits)[8],
+                                       unsigned mask) {
+    const float2 magic2 = make_float2(kRoundMagic, kRoundMagic);
+    const float2 nmagic2 = make_float2(-kRoundMagic, -kRoundMagic);
+    const float2 inv2 = make_float2(inv, inv);
+    bool slow = !(s >= 1.17549435e-38f);
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+        const float2 rq = __fmul2_rn(make_float2(v[2 * p], v[2 * p + 1]), inv2);
+        const float2 tt = __fadd2_rn(rq, magic2);
+        const float2 rr = __fadd2_rn(tt, nmagic2);
+        const float2 d = __ffma2_rn(rr, make_float2(-1.0f, -1.0f), rq);  // rq - rr, exact
+        slow |= !(fabsf(d.x) < 0.499f) | !(fabsf(d.y) < 0.499f);
+        bits[2 * p] = __float_as_uint(tt.x);
+        bits[2 * p + 1] = __float_as_uint(tt.y);
+    }
+    if (__any_sync(mask, slow)) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) bits[i] = quant_bits(v[i], s, inv, qmax);
+    }
+}
+
 // ---------------------------------------------- per-row quantize kernels --
 
 // One CTA per row.  Pass 1 reduces max|w| over the row, pass 2 re-reads the
@@ -69,11 +99,13 @@ __global__ void __launch_bounds__(kRowThreads) quant_rowwise_kernel(const T *__r
             for (int64_t c = 8 * (int64_t)threadIdx.x; c < k; c += 8 * (int64_t)blockDim.x) {
                 float v[8];
                 load8<T>(row + c, v);
+                uint32_t b[8];
+                quant8(v, s, inv, qmax, b, __activemask());
                 uint32_t lo = 0, hi = 0;
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
-                    lo |= (quant_bits(v[i], s, inv, qmax) & 0xFFu) << (8 * i);
-                    hi |= (quant_bits(v[i + 4], s, inv, qmax) & 0xFFu) << (8 * i);
+                    lo |= (b[i] & 0xFFu) << (8 * i);
+                    hi |= (b[i + 4] & 0xFFu) << (8 * i);
                 }
                 *reinterpret_cast<uint2 *>(qrow + c) = make_uint2(lo, hi);
             }
@@ -87,9 +119,11 @@ __global__ void __launch_bounds__(kRowThreads) quant_rowwise_kernel(const T *__r
             for (int64_t c = 8 * (int64_t)threadIdx.x; c < k; c += 8 * (int64_t)blockDim.x) {
                 float v[8];
                 load8<T>(row + c, v);
+                uint32_t b[8];
+                quant8(v, s, inv, qmax, b, __activemask());
                 uint32_t word = 0;
 #pragma unroll
-                for (int i = 0; i < 8; ++i) word |= (quant_bits(v[i], s, inv, qmax) & 15u) << (4 * i);
+                for (int i = 0; i < 8; ++i) word |= (b[i] & 15u) << (4 * i);
                 *reinterpret_cast<uint32_t *>(prow + c / 2) = word;
             }
         } else {
@@ -172,6 +206,66 @@ __global__ void __launch_bounds__(256) quant_group_kernel(const T *__restrict__ 
         }
     }
     if (nonfinite != nullptr && bad) *nonfinite = 1;
+}
+
+// Fast groupwise quantizer (16-byte-aligned rows, K % 8 == 0): same
+// thread/group mapping as quant_group_kernel, two 8-weight chunks in flight
+// per thread, one fmax per weight for the group max, non-finite detection by
+// a running fma(w, 0, acc) (NaN iff some w is NaN or +-Inf), and the packed
+// f32x2 quotients of quant8().  Bit-exact with quant_group_kernel (and the
+// reference) by construction.
+template <typename T, int L>
+__global__ void __launch_bounds__(256) quant_group_fast_kernel(const T *__restrict__ w, int64_t n, int64_t k,
+                                                               int64_t kp, uint8_t *__restrict__ packed,
+                                                               float *__restrict__ scales,
+                                                               int32_t *__restrict__ nonfinite) {
+    constexpr int C = 2;  // chunks per thread per iteration
+    const int64_t chunks_per_row = kp / 8;
+    const int64_t total = n * chunks_per_row;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;  // a multiple of 32 and of L
+    float fin = 0.0f;
+    for (int64_t t0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t0 - threadIdx.x % 32 < total;
+         t0 += C * stride) {
+        float v[C][8];
+        int64_t r[C], j[C];
+        bool live[C];
+#pragma unroll
+        for (int c = 0; c < C; ++c) {
+            const int64_t t = t0 + c * stride;
+            live[c] = t < total;
+            r[c] = live[c] ? t / chunks_per_row : 0;
+            j[c] = live[c] ? t - r[c] * chunks_per_row : 0;
+            if (live[c] && 8 * j[c] < k) {
+                load8<T>(w + r[c] * k + 8 * j[c], v[c]);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) v[c][i] = 0.0f;
+            }
+        }
+#pragma unroll
+        for (int c = 0; c < C; ++c) {
+            float mx = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                mx = fmaxf(mx, fabsf(v[c][i]));
+                fin = fmaf(v[c][i], 0.0f, fin);
+            }
+#pragma unroll
+            for (int o = L / 2; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            const float s = scale_from_max(mx, 7.0f);
+            const float inv = __frcp_rn(s);
+            uint32_t b[8];
+            quant8(v[c], s, inv, 7.0f, b, 0xffffffffu);
+            uint32_t word = 0;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) word |= (b[i] & 15u) << (4 * i);
+            if (live[c]) {
+                if ((j[c] % L) == 0) scales[r[c] * (chunks_per_row / L) + j[c] / L] = s;
+                *reinterpret_cast<uint32_t *>(packed + r[c] * (kp / 2) + 4 * j[c]) = word;
+            }
+        }
+    }
+    if (nonfinite != nullptr && fin != fin) *nonfinite = 1;
 }
 
 // Any even group size: one thread per (row, group), scalar loads.
@@ -320,7 +414,7 @@ int launch_group(const T *w, int64_t n, int64_t k, int g, uint8_t *packed, float
 #define OQ_G(LL)                                                                                   \
     case LL:                                                                                       \
         if (vec)                                                                                   \
-            quant_group_kernel<T, LL, true><<<(unsigned)blocks, threads, 0, st>>>(w, n, k, kp, packed, scales, flag); \
+            quant_group_fast_kernel<T, LL><<<(unsigned)blocks, threads, 0, st>>>(w, n, k, kp, packed, scales, flag); \
         else                                                                                       \
             quant_group_kernel<T, LL, false><<<(unsigned)blocks, threads, 0, st>>>(w, n, k, kp, packed, scales, flag); \
         break;
