@@ -1,6 +1,7 @@
 // Error state, version and device queries of the openquant_b200 C ABI.
 #include "oq_sm100.cuh"
 
+#include <map>
 #include <mutex>
 #include <vector>
 
@@ -39,6 +40,19 @@ int check_launch(const char *what) {
         set_error("%s: kernel launch failed: %s", what, cudaGetErrorString(err));
         return OQ_ERR_CUDA;
     }
+    return OQ_OK;
+}
+
+int allow_dynamic_smem(const void *kern, size_t bytes) {
+    static std::mutex mu;
+    static std::map<std::pair<const void *, int>, size_t> done;
+    int dev = 0;
+    OQ_CUDA(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = done.find({kern, dev});
+    if (it != done.end() && it->second >= bytes) return OQ_OK;
+    OQ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+    done[{kern, dev}] = bytes;
     return OQ_OK;
 }
 

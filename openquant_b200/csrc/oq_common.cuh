@@ -55,6 +55,9 @@ inline int dtype_size(int dtype) {
 
 // Number of SMs of the current device (cached per device).
 int sm_count();
+// Raises a kernel's dynamic shared-memory limit to `bytes` on the current
+// device (once per kernel, device and size; thread-safe).
+int allow_dynamic_smem(const void *kern, size_t bytes);
 
 __host__ __device__ inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 

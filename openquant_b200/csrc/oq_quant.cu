@@ -5,7 +5,10 @@
 // consecutive weights per thread, warp-shuffle max reductions, 4-/8-byte
 // packed stores.  Bit-exactness with the reference rests on oq::quant_bits()
 // (IEEE quotient, round-half-even) and oq::scale_from_max() (IEEE division).
-#include "oq_common.cuh"
+#include "oq_sm100.cuh"
+
+#include <algorithm>
+#include <type_traits>
 
 namespace oq {
 namespace {
@@ -31,11 +34,20 @@ __device__ __forceinline__ float block_max(float v, float *smem) {
     return r;
 }
 
+// Near-tie bound of the reciprocal fast paths.  With a normal scale s and
+// |v| <= max, r = fl(v * fl(1/s)) and the reference quotient fl(v / s) each
+// lie within 7 * 2^-23 of v/s, so |r - fl(v/s)| < 2^-19.  Their roundings
+// can only differ if a half-integer lies between them, i.e. if r is within
+// 2^-19 of a tie; |d| = |r - rint(r)| >= 0.5 - 2^-16 covers that 8x over.
+// The bound is tight so that a warp-wide vote rarely takes the exact path.
+constexpr float kNearTie = 0.5f - 1.0f / 65536.0f;
+constexpr float kNearTieSq = kNearTie * kNearTie;
+
 // Eight quotients q_i = clip(rint(fl(v_i / s)), -qmax, qmax) as the bit
 // patterns of (q_i + 1.5*2^23) (low byte / nibble = q_i), like quant_bits but
 // with packed f32x2 arithmetic: r = v * (1/s), t = r + 1.5*2^23 (round half
 // to even), d = r - (t - 1.5*2^23).  When any lane of `mask` has a quotient
-// within 1e-3 of a tie (|d| >= 0.499) or a scale that is not a normal float
+// near a tie (|d| >= kNearTie) or a scale that is not a normal float
 // (zero-substituted, subnormal, NaN), those lanes redo all eight with
 // quant_bits (IEEE quotient, clipping, NaN -> 0).  For a normal scale derived
 // from the values' max, |v/s| <= qmax up to a few ulps, so no clip is needed.
@@ -51,7 +63,7 @@ __device__ __forceinline__ void quant8(const float (&v)[8], float s, float inv, 
         const float2 tt = __fadd2_rn(rq, magic2);
         const float2 rr = __fadd2_rn(tt, nmagic2);
         const float2 d = __ffma2_rn(rr, make_float2(-1.0f, -1.0f), rq);  // rq - rr, exact
-        slow |= !(fabsf(d.x) < 0.499f) | !(fabsf(d.y) < 0.499f);
+        slow |= !(fabsf(d.x) < kNearTie) | !(fabsf(d.y) < kNearTie);
         bits[2 * p] = __float_as_uint(tt.x);
         bits[2 * p + 1] = __float_as_uint(tt.y);
     }
@@ -268,6 +280,282 @@ __global__ void __launch_bounds__(256) quant_group_fast_kernel(const T *__restri
     if (nonfinite != nullptr && fin != fin) *nonfinite = 1;
 }
 
+// ------------------------------------------- streaming groupwise quantize --
+//
+// For K % g == 0 (no padding) the weights, the packed nibbles and the scales
+// are three flat arrays: weight e goes to byte e/2 and scale e/g.  The
+// stream kernel walks the weights in 16 KB tiles: one producer lane keeps a
+// ring of tiles in flight with 1-D bulk copies into shared memory (mbarrier
+// completion, bounded waits), and CW consumer warps quantize each tile with
+// every thread owning CPT consecutive 8-weight chunks of one group.
+
+constexpr int kStreamTile = 16384;  // bytes per stage
+
+// Raw 8-weight chunks: the integer |w| max (|w| bit patterns of IEEE types
+// order like their values, Inf and NaN above every finite value) and the
+// conversion of the raw words to f32.
+template <typename T> struct Chunk;
+template <> struct Chunk<__nv_bfloat16> {
+    static constexpr int kWords = 4;
+    static constexpr uint32_t kNonFinite = 0x7F80u;
+    static __device__ __forceinline__ uint32_t absmax(const uint32_t *x) {
+        return __vmaxu2(__vmaxu2(x[0] & 0x7FFF7FFFu, x[1] & 0x7FFF7FFFu),
+                        __vmaxu2(x[2] & 0x7FFF7FFFu, x[3] & 0x7FFF7FFFu));
+    }
+    static __device__ __forceinline__ uint32_t combine(uint32_t a, uint32_t b) { return __vmaxu2(a, b); }
+    static __device__ __forceinline__ uint32_t fold(uint32_t m) { return max(m & 0xFFFFu, m >> 16); }
+    static __device__ __forceinline__ float to_f32(uint32_t m) { return __uint_as_float(m << 16); }
+    static __device__ __forceinline__ void unpack(const uint32_t *x, float (&v)[8]) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            v[2 * i] = __uint_as_float(x[i] << 16);
+            v[2 * i + 1] = __uint_as_float(x[i] & 0xFFFF0000u);
+        }
+    }
+};
+template <> struct Chunk<__half> {
+    static constexpr int kWords = 4;
+    static constexpr uint32_t kNonFinite = 0x7C00u;
+    static __device__ __forceinline__ uint32_t absmax(const uint32_t *x) { return Chunk<__nv_bfloat16>::absmax(x); }
+    static __device__ __forceinline__ uint32_t combine(uint32_t a, uint32_t b) { return __vmaxu2(a, b); }
+    static __device__ __forceinline__ uint32_t fold(uint32_t m) { return max(m & 0xFFFFu, m >> 16); }
+    static __device__ __forceinline__ float to_f32(uint32_t m) { return __half2float(__ushort_as_half((unsigned short)m)); }
+    static __device__ __forceinline__ void unpack(const uint32_t *x, float (&v)[8]) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            __half2 h;
+            memcpy(&h, &x[i], 4);
+            const float2 f = __half22float2(h);
+            v[2 * i] = f.x;
+            v[2 * i + 1] = f.y;
+        }
+    }
+};
+template <> struct Chunk<float> {
+    static constexpr int kWords = 8;
+    static constexpr uint32_t kNonFinite = 0x7F800000u;
+    static __device__ __forceinline__ uint32_t absmax(const uint32_t *x) {
+        uint32_t m = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) m = max(m, x[i] & 0x7FFFFFFFu);
+        return m;
+    }
+    static __device__ __forceinline__ uint32_t combine(uint32_t a, uint32_t b) { return max(a, b); }
+    static __device__ __forceinline__ uint32_t fold(uint32_t m) { return m; }
+    static __device__ __forceinline__ float to_f32(uint32_t m) { return __uint_as_float(m); }
+    static __device__ __forceinline__ void unpack(const uint32_t *x, float (&v)[8]) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(x[i]);
+    }
+};
+
+// Packed nibbles of eight weights for a normal scale (1/s = inv).  The
+// quotients are paired (v_i, v_i+4) for f32x2 arithmetic:
+//   r = v * inv;  rr = (r + 1.5*2^23) - 1.5*2^23   (round half to even)
+//   d = r - rr;   e = fma(d, d, -kNearTie^2)      (e >= 0 iff |d| >= kNearTie:
+//                                                 one rounding keeps the sign)
+// The sign bits of e are ANDed into *allneg (it stays negative while no
+// quotient is near a tie).  The rounded values rr (integers in [-7, 7]) are
+// combined exactly as sum_i (rr_i + 8) * 16^i in two 16-bit halves, whose
+// float bit patterns after adding 1.5*2^23 carry them in the low bits;
+// XOR 8 per nibble turns the offset-8 code into two's complement.
+__device__ __forceinline__ uint32_t pack8_fast(const float (&v)[8], float2 inv2, int &allneg) {
+    const float2 magic2 = make_float2(kRoundMagic, kRoundMagic);
+    const float2 nmagic2 = make_float2(-kRoundMagic, -kRoundMagic);
+    float2 rr[4];
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+        const float2 rq = __fmul2_rn(make_float2(v[p], v[p + 4]), inv2);
+        rr[p] = __fadd2_rn(__fadd2_rn(rq, magic2), nmagic2);
+        const float2 d = __ffma2_rn(rr[p], make_float2(-1.0f, -1.0f), rq);
+        const float2 e = __ffma2_rn(d, d, make_float2(-kNearTieSq, -kNearTieSq));
+        allneg &= __float_as_int(e.x) & __float_as_int(e.y);
+    }
+    const float2 c16 = make_float2(16.0f, 16.0f);
+    const float2 lo = __ffma2_rn(rr[1], c16, rr[0]);  // (q0 + 16 q1, q4 + 16 q5)
+    const float2 hi = __ffma2_rn(rr[3], c16, rr[2]);  // (q2 + 16 q3, q6 + 16 q7)
+    const float off = kRoundMagic + 34952.0f;         // 1.5*2^23 + 0x8888
+    const float2 h = __fadd2_rn(__ffma2_rn(hi, make_float2(256.0f, 256.0f), lo), make_float2(off, off));
+    return __byte_perm(__float_as_uint(h.x), __float_as_uint(h.y), 0x5410) ^ 0x88888888u;
+}
+
+// Packed nibbles of eight 16-bit (bf16 / fp16) weights, quotients by one
+// correction step of the reciprocal product (Markstein's division
+// correction): q0 = v * y, r = fma(-q0, s, v), q = fma(r, y, q0), with
+// y = RN(1/s).  For every pair of finite 16-bit weights v and max m >= |v|
+// whose scale s = fl(m / 7) is at least 2^-100, rint(q) equals
+// rint(fl(v / s)); the exhaustive check over all such pairs is
+// test_quant_stream_gpu.py::test_stream_16bit_fast_path_exhaustive.  Ties of
+// the quotient are therefore decided like the IEEE quotient's, with no
+// near-tie test.  Packing as in pack8_fast.
+__device__ __forceinline__ uint32_t pack8_corrected(const float (&v)[8], float2 s2, float2 y2) {
+    const float2 magic2 = make_float2(kRoundMagic, kRoundMagic);
+    const float2 nmagic2 = make_float2(-kRoundMagic, -kRoundMagic);
+    const float2 ns2 = make_float2(-s2.x, -s2.y);
+    float2 rr[4];
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+        const float2 w2 = make_float2(v[p], v[p + 4]);
+        const float2 q0 = __fmul2_rn(w2, y2);
+        const float2 q = __ffma2_rn(__ffma2_rn(q0, ns2, w2), y2, q0);
+        rr[p] = __fadd2_rn(__fadd2_rn(q, magic2), nmagic2);
+    }
+    const float2 c16 = make_float2(16.0f, 16.0f);
+    const float2 lo = __ffma2_rn(rr[1], c16, rr[0]);
+    const float2 hi = __ffma2_rn(rr[3], c16, rr[2]);
+    const float off = kRoundMagic + 34952.0f;
+    const float2 h = __fadd2_rn(__ffma2_rn(hi, make_float2(256.0f, 256.0f), lo), make_float2(off, off));
+    return __byte_perm(__float_as_uint(h.x), __float_as_uint(h.y), 0x5410) ^ 0x88888888u;
+}
+
+// fl(m / 7) for m > 0 by the same correction with RN(1/7); equal to the IEEE
+// quotient for every positive finite float m (checked exhaustively on the
+// GPU over all 2^31 - 2^23 of them); scale 1 for m == 0 as scale_from_max.
+__device__ __forceinline__ float scale7(float m) {
+    constexpr float kInv7 = 1.0f / 7.0f;
+    const float q0 = __fmul_rn(m, kInv7);
+    const float q = __fmaf_rn(__fmaf_rn(-q0, 7.0f, m), kInv7, q0);
+    return m == 0.0f ? 1.0f : q;
+}
+
+__device__ __forceinline__ uint32_t pack8_exact(const float (&v)[8], float s, float inv) {
+    uint32_t word = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) word |= (quant_bits(v[i], s, inv, 7.0f) & 15u) << (4 * i);
+    return word;
+}
+
+template <typename T, int G, int CW, int CPT>
+__global__ void __launch_bounds__((CW + 1) * 32)
+    quant_group_stream_kernel(const T *__restrict__ w, int64_t total, int nstages, uint8_t *__restrict__ packed,
+                              float *__restrict__ scales, int32_t *__restrict__ nonfinite) {
+    using C = Chunk<T>;
+    constexpr int E = kStreamTile / (int)sizeof(T);  // weights per tile
+    constexpr int L = G / (8 * CPT);                 // lanes per group
+    constexpr int V = CPT * C::kWords / 4;           // 16-byte vectors per thread
+    constexpr int VPC = C::kWords / 4;               // vectors per chunk
+    constexpr int SLOTS = E / (8 * CPT);
+    constexpr int PASSES = SLOTS / (CW * 32);
+    static_assert(L >= 1 && L * 8 * CPT == G, "group must split into whole thread shares");
+    static_assert(PASSES >= 1 && PASSES * CW * 32 == SLOTS, "tile must split evenly over the consumer threads");
+    static_assert(V == 1 || V == 2 || V == 4, "unsupported vectors per thread");
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + (size_t)nstages * kStreamTile);
+    uint64_t *empty = full + nstages;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t tiles = (total + E - 1) / E;
+    const int64_t mine = (int64_t)blockIdx.x < tiles ? (tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < nstages; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], CW);
+        }
+        fence_barrier_init();
+    }
+    __syncthreads();
+
+    if (warp == CW) {  // ------------------------------------ producer
+        if (lane == 0) {
+            for (int64_t pos = 0; pos < mine; ++pos) {
+                const int slot = (int)(pos % nstages);
+                const int64_t round = pos / nstages;
+                if (round > 0 && !mbar_wait(&empty[slot], (uint32_t)((round - 1) & 1))) break;
+                const int64_t base = ((int64_t)blockIdx.x + pos * gridDim.x) * E;
+                const uint32_t bytes = (uint32_t)(min((int64_t)E, total - base) * (int64_t)sizeof(T));
+                mbar_arrive_expect_tx(&full[slot], bytes);
+                bulk_load_1d(smem + (size_t)slot * kStreamTile, w + base, bytes, &full[slot]);
+            }
+        }
+        return;
+    }
+
+    // Vector q of a thread is read from position q ^ x, x = lane bits that
+    // put the 8 lanes of a quarter-warp on distinct 16-byte bank groups.
+    const int x = V == 1 ? 0 : V == 2 ? (lane >> 2) & 1 : (lane >> 1) & 3;
+    const int cx = x / VPC;  // chunk permutation
+    const bool halves = VPC == 2 && (x & 1);  // f32: the two halves of every chunk swapped
+    bool bad = false;
+    for (int64_t pos = 0; pos < mine; ++pos) {
+        const int slot = (int)(pos % nstages);
+        if (!__all_sync(0xffffffffu, mbar_wait(&full[slot], (uint32_t)((pos / nstages) & 1)))) break;
+        const int64_t base = ((int64_t)blockIdx.x + pos * gridDim.x) * E;
+        const int valid = (int)min((int64_t)E, total - base);
+        const uint8_t *tile = smem + (size_t)slot * kStreamTile;
+#pragma unroll
+        for (int p = 0; p < PASSES; ++p) {
+            const int u = p * CW * 32 + (int)threadIdx.x;
+            const int e0 = u * 8 * CPT;
+            const bool live = e0 < valid;  // groups lie wholly inside or outside [0, valid)
+            uint32_t r[V * 4];
+#pragma unroll
+            for (int q = 0; q < V; ++q) {
+                uint4 t = make_uint4(0, 0, 0, 0);
+                if (live) t = *reinterpret_cast<const uint4 *>(tile + (size_t)(u * V + (q ^ x)) * 16);
+                r[4 * q] = t.x, r[4 * q + 1] = t.y, r[4 * q + 2] = t.z, r[4 * q + 3] = t.w;
+            }
+            uint32_t mb = C::absmax(r);
+#pragma unroll
+            for (int c = 1; c < CPT; ++c) mb = C::combine(mb, C::absmax(r + c * C::kWords));
+            mb = C::fold(mb);
+#pragma unroll
+            for (int o = L / 2; o > 0; o >>= 1) mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, o));
+            bad |= mb >= C::kNonFinite;
+            const float s = scale7(C::to_f32(mb));  // NaN / Inf for a non-finite max: exact path
+            const float inv = __frcp_rn(s);
+            int allneg = -1;
+            uint32_t wd[CPT];
+#pragma unroll
+            for (int c = 0; c < CPT; ++c) {
+                float v[8];
+                C::unpack(r + c * C::kWords, v);
+                if (sizeof(T) == 2)
+                    wd[c] = pack8_corrected(v, make_float2(s, s), make_float2(inv, inv));
+                else
+                    wd[c] = pack8_fast(v, make_float2(inv, inv), allneg);
+            }
+            // 16-bit weights: exact for scales in [2^-100, max float]; fp32:
+            // exact unless a quotient is near a tie or the scale is not normal.
+            const bool slow = sizeof(T) == 2 ? !(s >= 0x1p-100f && s <= 3.40282347e38f)
+                                             : (allneg >= 0 || !(s >= 1.17549435e-38f && s <= 3.40282347e38f));
+            if (__any_sync(0xffffffffu, slow)) {
+#pragma unroll
+                for (int c = 0; c < CPT; ++c) {
+                    float v[8];
+                    C::unpack(r + c * C::kWords, v);
+                    wd[c] = pack8_exact(v, s, inv);
+                }
+            }
+            if (halves) {
+#pragma unroll
+                for (int c = 0; c < CPT; ++c) wd[c] = __byte_perm(wd[c], 0, 0x1032);
+            }
+            // Undo the chunk permutation: word c was computed from chunk c ^ cx.
+            if (CPT >= 2 && (cx & 1)) {
+#pragma unroll
+                for (int c = 0; c < CPT; c += 2) { const uint32_t t = wd[c]; wd[c] = wd[c + 1]; wd[c + 1] = t; }
+            }
+            if (CPT >= 4 && (cx & 2)) {
+#pragma unroll
+                for (int c = 0; c < CPT; c += 4) {
+                    uint32_t t = wd[c]; wd[c] = wd[c + 2]; wd[c + 2] = t;
+                    t = wd[c + 1]; wd[c + 1] = wd[c + 3]; wd[c + 3] = t;
+                }
+            }
+            if (live) {
+                uint8_t *dst = packed + (base + e0) / 2;
+                if (CPT == 1) *reinterpret_cast<uint32_t *>(dst) = wd[0];
+                if (CPT == 2) *reinterpret_cast<uint2 *>(dst) = make_uint2(wd[0], wd[1 % CPT]);
+                if (CPT == 4) *reinterpret_cast<uint4 *>(dst) = make_uint4(wd[0], wd[1 % CPT], wd[2 % CPT], wd[3 % CPT]);
+                if (lane % L == 0) scales[(base + e0) / G] = s;
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
+    }
+    if (nonfinite != nullptr && bad) *nonfinite = 1;
+}
+
 // Any even group size: one thread per (row, group), scalar loads.
 template <typename T>
 __global__ void quant_group_generic_kernel(const T *__restrict__ w, int64_t n, int64_t k, int64_t kp, int g,
@@ -399,9 +687,63 @@ int launch_rowwise(const T *w, int64_t n, int64_t k, uint8_t *out, float *scales
     return check_launch("quantize (per-row)");
 }
 
+// Streaming quantizer launch for K % g == 0 (g a power of two in [8, 256]),
+// 16-byte-aligned weights and 4*CPT-byte-aligned output; returns
+// OQ_ERR_UNSUPPORTED when the shape or alignment does not qualify.
+constexpr int kStreamWarps = 8;
+
+template <typename T, int CPT>
+int launch_group_stream_cpt(const T *w, int64_t total, int g, uint8_t *packed, float *scales, int32_t *flag,
+                            int nstages, int ctas_per_sm, cudaStream_t st) {
+    constexpr int E = kStreamTile / (int)sizeof(T);
+    const int64_t tiles = cdiv(total, E);
+    const int64_t grid = std::min<int64_t>(tiles, (int64_t)sm_count() * ctas_per_sm);
+    const size_t smem = (size_t)nstages * (kStreamTile + 16);
+    const void *kern = nullptr;
+    switch (g) {
+#define OQ_S(GG)                                                                                          \
+    case GG:                                                                                              \
+        if constexpr (GG >= 8 * CPT) kern = reinterpret_cast<const void *>(&quant_group_stream_kernel<T, GG, kStreamWarps, CPT>); \
+        break;
+        OQ_S(8) OQ_S(16) OQ_S(32) OQ_S(64) OQ_S(128) OQ_S(256)
+#undef OQ_S
+        default: break;
+    }
+    if (kern == nullptr) return OQ_ERR_UNSUPPORTED;
+    const int rc = allow_dynamic_smem(kern, smem);
+    if (rc != OQ_OK) return rc;
+    void *args[] = {(void *)&w, (void *)&total, (void *)&nstages, (void *)&packed, (void *)&scales, (void *)&flag};
+    OQ_CUDA(cudaLaunchKernel(kern, dim3((unsigned)grid), dim3((kStreamWarps + 1) * 32), args, smem, st));
+    return OQ_OK;
+}
+
+template <typename T>
+int launch_group_stream(const T *w, int64_t n, int64_t k, int g, uint8_t *packed, float *scales, int32_t *flag,
+                        cudaStream_t st, int nstages = 4, int ctas_per_sm = 3, int cpt = 0) {
+    if constexpr (std::is_same<T, double>::value) {
+        return OQ_ERR_UNSUPPORTED;
+    } else {
+        constexpr int kMaxCpt = sizeof(T) == 4 ? 2 : 4;
+        if (g < 8 || g > 256 || (g & (g - 1)) != 0 || k % g != 0 || !aligned(w, 16)) return OQ_ERR_UNSUPPORTED;
+        if (cpt == 0) cpt = std::min(kMaxCpt, g / 8);  // 16-bit: 32 weights per thread for g >= 32
+        if (cpt > kMaxCpt || cpt > g / 8 || !aligned(packed, 4 * cpt)) return OQ_ERR_UNSUPPORTED;
+        const int64_t total = n * k;
+        if (cpt == 1) return launch_group_stream_cpt<T, 1>(w, total, g, packed, scales, flag, nstages, ctas_per_sm, st);
+        if (cpt == 2) return launch_group_stream_cpt<T, 2>(w, total, g, packed, scales, flag, nstages, ctas_per_sm, st);
+        if constexpr (kMaxCpt >= 4) {
+            if (cpt == 4) return launch_group_stream_cpt<T, 4>(w, total, g, packed, scales, flag, nstages, ctas_per_sm, st);
+        }
+        return OQ_ERR_UNSUPPORTED;
+    }
+}
+
 template <typename T>
 int launch_group(const T *w, int64_t n, int64_t k, int g, uint8_t *packed, float *scales, int32_t *flag,
                  cudaStream_t st) {
+    {
+        const int rc = launch_group_stream(w, n, k, g, packed, scales, flag, st);
+        if (rc != OQ_ERR_UNSUPPORTED) return rc == OQ_OK ? check_launch("quantize_int4_groupwise") : rc;
+    }
     const int64_t kp = cdiv(k, g) * g;
     const bool fast = g >= 8 && g <= 256 && (g & (g - 1)) == 0 && aligned(packed, 4);
     const bool vec = (k % 8 == 0) && aligned(w, 16);

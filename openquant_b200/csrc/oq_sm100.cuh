@@ -109,6 +109,14 @@ __device__ __forceinline__ void tma_load_2d(void *smem_dst, const CUtensorMap *m
         : "memory");
 }
 
+// 1-D bulk copy of `bytes` (a multiple of 16; both addresses 16-byte aligned)
+// from global into this CTA's shared memory, completing on the mbarrier.
+__device__ __forceinline__ void bulk_load_1d(void *smem_dst, const void *gsrc, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(gsrc)), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
 // 4-byte asynchronous global -> shared copy (cp.async), and an mbarrier
 // arrival that fires when all of this thread's earlier cp.async copies have
 // landed (counts toward the barrier's expected arrivals).
