@@ -297,6 +297,7 @@ constexpr int kStreamTile = 16384;  // bytes per stage
 template <typename T> struct Chunk;
 template <> struct Chunk<__nv_bfloat16> {
     static constexpr int kWords = 4;
+    static constexpr bool kCorrected = true;  // quot8's corrected quotient is exact for 16-bit weights
     static constexpr uint32_t kNonFinite = 0x7F80u;
     static __device__ __forceinline__ uint32_t absmax(const uint32_t *x) {
         return __vmaxu2(__vmaxu2(x[0] & 0x7FFF7FFFu, x[1] & 0x7FFF7FFFu),
@@ -315,6 +316,7 @@ template <> struct Chunk<__nv_bfloat16> {
 };
 template <> struct Chunk<__half> {
     static constexpr int kWords = 4;
+    static constexpr bool kCorrected = true;
     static constexpr uint32_t kNonFinite = 0x7C00u;
     static __device__ __forceinline__ uint32_t absmax(const uint32_t *x) { return Chunk<__nv_bfloat16>::absmax(x); }
     static __device__ __forceinline__ uint32_t combine(uint32_t a, uint32_t b) { return __vmaxu2(a, b); }
@@ -333,6 +335,7 @@ template <> struct Chunk<__half> {
 };
 template <> struct Chunk<float> {
     static constexpr int kWords = 8;
+    static constexpr bool kCorrected = false;
     static constexpr uint32_t kNonFinite = 0x7F800000u;
     static __device__ __forceinline__ uint32_t absmax(const uint32_t *x) {
         uint32_t m = 0;
@@ -349,28 +352,45 @@ template <> struct Chunk<float> {
     }
 };
 
-// Packed nibbles of eight weights for a normal scale (1/s = inv).  The
-// quotients are paired (v_i, v_i+4) for f32x2 arithmetic:
-//   r = v * inv;  rr = (r + 1.5*2^23) - 1.5*2^23   (round half to even)
-//   d = r - rr;   e = fma(d, d, -kNearTie^2)      (e >= 0 iff |d| >= kNearTie:
-//                                                 one rounding keeps the sign)
-// The sign bits of e are ANDed into *allneg (it stays negative while no
-// quotient is near a tie).  The rounded values rr (integers in [-7, 7]) are
-// combined exactly as sum_i (rr_i + 8) * 16^i in two 16-bit halves, whose
-// float bit patterns after adding 1.5*2^23 carry them in the low bits;
-// XOR 8 per nibble turns the offset-8 code into two's complement.
-__device__ __forceinline__ uint32_t pack8_fast(const float (&v)[8], float2 inv2, int &allneg) {
+// Rounded quotients of eight weights, rr_i = rint(q_i) as floats, in the
+// pair layout rr[p] = (element p, element p + 4) of the f32x2 arithmetic.
+//
+// CORRECTED (16-bit weights): one correction step of the reciprocal product
+// (Markstein's division correction), q0 = v * y, r = fma(-q0, s, v),
+// q = fma(r, y, q0) with y = RN(1/s).  For every pair of finite 16-bit
+// weights v and max m >= |v| whose scale s = fl(m / qmax) (qmax 7 or 127) is
+// at least 2^-100, rint(q) equals rint(fl(v / s)) -- checked over all such
+// pairs on the GPU, and by test_quant_stream_gpu.py for the kernels -- so
+// ties of the quotient are decided like the IEEE quotient's.
+//
+// Otherwise (fp32 weights): q = v * y, and the sign bits of
+// e = fma(d, d, -kNearTie^2), d = q - rint(q), are ANDed into *allneg, which
+// stays negative while no quotient is near a tie (one rounding keeps the sign
+// of d*d - kNearTie^2).  rint is (q + 1.5*2^23) - 1.5*2^23, round half to even.
+template <bool CORRECTED>
+__device__ __forceinline__ void quot8(const float (&v)[8], float2 s2, float2 y2, float2 (&rr)[4], int &allneg) {
     const float2 magic2 = make_float2(kRoundMagic, kRoundMagic);
     const float2 nmagic2 = make_float2(-kRoundMagic, -kRoundMagic);
-    float2 rr[4];
 #pragma unroll
     for (int p = 0; p < 4; ++p) {
-        const float2 rq = __fmul2_rn(make_float2(v[p], v[p + 4]), inv2);
-        rr[p] = __fadd2_rn(__fadd2_rn(rq, magic2), nmagic2);
-        const float2 d = __ffma2_rn(rr[p], make_float2(-1.0f, -1.0f), rq);
-        const float2 e = __ffma2_rn(d, d, make_float2(-kNearTieSq, -kNearTieSq));
-        allneg &= __float_as_int(e.x) & __float_as_int(e.y);
+        const float2 w2 = make_float2(v[p], v[p + 4]);
+        float2 q = __fmul2_rn(w2, y2);
+        if (CORRECTED) q = __ffma2_rn(__ffma2_rn(q, make_float2(-s2.x, -s2.y), w2), y2, q);
+        rr[p] = __fadd2_rn(__fadd2_rn(q, magic2), nmagic2);
+        if (!CORRECTED) {
+            const float2 d = __ffma2_rn(rr[p], make_float2(-1.0f, -1.0f), q);
+            const float2 e = __ffma2_rn(d, d, make_float2(-kNearTieSq, -kNearTieSq));
+            allneg &= __float_as_int(e.x) & __float_as_int(e.y);
+        }
     }
+}
+
+// Eight rounded quotients in [-7, 7] -> one word of nibbles (element i in
+// bits 4i..4i+3, two's complement).  sum_i (rr_i + 8) * 16^i is formed
+// exactly in two 16-bit halves, whose float bit patterns after adding
+// 1.5*2^23 carry them in the low bits; XOR 8 per nibble turns the offset-8
+// code into two's complement.
+__device__ __forceinline__ uint32_t nibbles8(const float2 (&rr)[4]) {
     const float2 c16 = make_float2(16.0f, 16.0f);
     const float2 lo = __ffma2_rn(rr[1], c16, rr[0]);  // (q0 + 16 q1, q4 + 16 q5)
     const float2 hi = __ffma2_rn(rr[3], c16, rr[2]);  // (q2 + 16 q3, q6 + 16 q7)
@@ -379,43 +399,34 @@ __device__ __forceinline__ uint32_t pack8_fast(const float (&v)[8], float2 inv2,
     return __byte_perm(__float_as_uint(h.x), __float_as_uint(h.y), 0x5410) ^ 0x88888888u;
 }
 
-// Packed nibbles of eight 16-bit (bf16 / fp16) weights, quotients by one
-// correction step of the reciprocal product (Markstein's division
-// correction): q0 = v * y, r = fma(-q0, s, v), q = fma(r, y, q0), with
-// y = RN(1/s).  For every pair of finite 16-bit weights v and max m >= |v|
-// whose scale s = fl(m / 7) is at least 2^-100, rint(q) equals
-// rint(fl(v / s)); the exhaustive check over all such pairs is
-// test_quant_stream_gpu.py::test_stream_16bit_fast_path_exhaustive.  Ties of
-// the quotient are therefore decided like the IEEE quotient's, with no
-// near-tie test.  Packing as in pack8_fast.
-__device__ __forceinline__ uint32_t pack8_corrected(const float (&v)[8], float2 s2, float2 y2) {
-    const float2 magic2 = make_float2(kRoundMagic, kRoundMagic);
-    const float2 nmagic2 = make_float2(-kRoundMagic, -kRoundMagic);
-    const float2 ns2 = make_float2(-s2.x, -s2.y);
-    float2 rr[4];
-#pragma unroll
-    for (int p = 0; p < 4; ++p) {
-        const float2 w2 = make_float2(v[p], v[p + 4]);
-        const float2 q0 = __fmul2_rn(w2, y2);
-        const float2 q = __ffma2_rn(__ffma2_rn(q0, ns2, w2), y2, q0);
-        rr[p] = __fadd2_rn(__fadd2_rn(q, magic2), nmagic2);
-    }
-    const float2 c16 = make_float2(16.0f, 16.0f);
-    const float2 lo = __ffma2_rn(rr[1], c16, rr[0]);
-    const float2 hi = __ffma2_rn(rr[3], c16, rr[2]);
-    const float off = kRoundMagic + 34952.0f;
-    const float2 h = __fadd2_rn(__ffma2_rn(hi, make_float2(256.0f, 256.0f), lo), make_float2(off, off));
-    return __byte_perm(__float_as_uint(h.x), __float_as_uint(h.y), 0x5410) ^ 0x88888888u;
+// Eight rounded quotients in [-127, 127] -> eight int8 bytes, the same way
+// with offset 128 per byte.
+__device__ __forceinline__ uint2 bytes8(const float2 (&rr)[4]) {
+    const float2 c256 = make_float2(256.0f, 256.0f);
+    const float off = kRoundMagic + 32896.0f;  // 1.5*2^23 + 0x8080
+    const float2 lo = __fadd2_rn(__ffma2_rn(rr[1], c256, rr[0]), make_float2(off, off));  // elements (0,1), (4,5)
+    const float2 hi = __fadd2_rn(__ffma2_rn(rr[3], c256, rr[2]), make_float2(off, off));  // elements (2,3), (6,7)
+    return make_uint2(__byte_perm(__float_as_uint(lo.x), __float_as_uint(hi.x), 0x5410) ^ 0x80808080u,
+                      __byte_perm(__float_as_uint(lo.y), __float_as_uint(hi.y), 0x5410) ^ 0x80808080u);
 }
 
-// fl(m / 7) for m > 0 by the same correction with RN(1/7); equal to the IEEE
+// fl(m / Q) for m > 0 by the same correction with RN(1/Q); equal to the IEEE
 // quotient for every positive finite float m (checked exhaustively on the
-// GPU over all 2^31 - 2^23 of them); scale 1 for m == 0 as scale_from_max.
-__device__ __forceinline__ float scale7(float m) {
-    constexpr float kInv7 = 1.0f / 7.0f;
-    const float q0 = __fmul_rn(m, kInv7);
-    const float q = __fmaf_rn(__fmaf_rn(-q0, 7.0f, m), kInv7, q0);
+// GPU over all 2^31 - 2^23 of them, Q = 7 and 127); scale 1 for m == 0 as
+// scale_from_max, NaN / Inf for a non-finite m.
+template <int Q> __device__ __forceinline__ float scale_q(float m) {
+    constexpr float kInv = 1.0f / (float)Q;
+    const float q0 = __fmul_rn(m, kInv);
+    const float q = __fmaf_rn(__fmaf_rn(-q0, (float)Q, m), kInv, q0);
     return m == 0.0f ? 1.0f : q;
+}
+
+// Does the fast path of quot8 decide every quotient exactly?  16-bit weights:
+// for scales in [2^-100, max float]; fp32: for normal scales with no quotient
+// near a tie.
+template <bool CORRECTED> __device__ __forceinline__ bool quot8_exact(float s, int allneg) {
+    if (CORRECTED) return s >= 0x1p-100f && s <= 3.40282347e38f;
+    return allneg < 0 && s >= 1.17549435e-38f && s <= 3.40282347e38f;
 }
 
 __device__ __forceinline__ uint32_t pack8_exact(const float (&v)[8], float s, float inv) {
@@ -423,6 +434,16 @@ __device__ __forceinline__ uint32_t pack8_exact(const float (&v)[8], float s, fl
 #pragma unroll
     for (int i = 0; i < 8; ++i) word |= (quant_bits(v[i], s, inv, 7.0f) & 15u) << (4 * i);
     return word;
+}
+
+__device__ __forceinline__ uint2 bytes8_exact(const float (&v)[8], float s, float inv) {
+    uint32_t lo = 0, hi = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        lo |= (quant_bits(v[i], s, inv, 127.0f) & 0xFFu) << (8 * i);
+        hi |= (quant_bits(v[i + 4], s, inv, 127.0f) & 0xFFu) << (8 * i);
+    }
+    return make_uint2(lo, hi);
 }
 
 template <typename T, int G, int CW, int CPT>
@@ -501,24 +522,19 @@ __global__ void __launch_bounds__((CW + 1) * 32)
 #pragma unroll
             for (int o = L / 2; o > 0; o >>= 1) mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, o));
             bad |= mb >= C::kNonFinite;
-            const float s = scale7(C::to_f32(mb));  // NaN / Inf for a non-finite max: exact path
+            const float s = scale_q<7>(C::to_f32(mb));  // NaN / Inf for a non-finite max: exact path
             const float inv = __frcp_rn(s);
             int allneg = -1;
             uint32_t wd[CPT];
 #pragma unroll
             for (int c = 0; c < CPT; ++c) {
                 float v[8];
+                float2 rr[4];
                 C::unpack(r + c * C::kWords, v);
-                if (sizeof(T) == 2)
-                    wd[c] = pack8_corrected(v, make_float2(s, s), make_float2(inv, inv));
-                else
-                    wd[c] = pack8_fast(v, make_float2(inv, inv), allneg);
+                quot8<C::kCorrected>(v, make_float2(s, s), make_float2(inv, inv), rr, allneg);
+                wd[c] = nibbles8(rr);
             }
-            // 16-bit weights: exact for scales in [2^-100, max float]; fp32:
-            // exact unless a quotient is near a tie or the scale is not normal.
-            const bool slow = sizeof(T) == 2 ? !(s >= 0x1p-100f && s <= 3.40282347e38f)
-                                             : (allneg >= 0 || !(s >= 1.17549435e-38f && s <= 3.40282347e38f));
-            if (__any_sync(0xffffffffu, slow)) {
+            if (__any_sync(0xffffffffu, !quot8_exact<C::kCorrected>(s, allneg))) {
 #pragma unroll
                 for (int c = 0; c < CPT; ++c) {
                     float v[8];
@@ -554,6 +570,119 @@ __global__ void __launch_bounds__((CW + 1) * 32)
         if (lane == 0) mbar_arrive(&empty[slot]);
     }
     if (nonfinite != nullptr && bad) *nonfinite = 1;
+}
+
+// ------------------------------------------------ streaming per-row quantize --
+//
+// Per-row INT8 / INT4 (flat packing) for K % 8 == 0: a stage holds R whole
+// rows (one 1-D bulk copy of R*K weights), so each weight leaves HBM once.
+// All CW consumer warps work on one row at a time: pass 1 reduces the
+// integer |w| max from shared memory (warp shuffles, then one named barrier
+// over a double-buffered per-warp array), pass 2 quantizes from shared
+// memory and stores 8 (INT8) or 4 (INT4) bytes per 8 weights.  With K even,
+// row r of the flat INT4 packing is bytes [r*K/2, (r+1)*K/2).
+template <typename T, int BITS, int CW>
+__global__ void __launch_bounds__((CW + 1) * 32)
+    quant_rowwise_stream_kernel(const T *__restrict__ w, int64_t n, int k, int rows_per_stage, int stage_bytes,
+                                int nstages, uint8_t *__restrict__ out, float *__restrict__ scales) {
+    using C = Chunk<T>;
+    constexpr int Q = BITS == 8 ? 127 : 7;
+    constexpr int VPC = C::kWords / 4;  // 16-byte vectors per 8-weight chunk
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ uint32_t red[2][CW];
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + (size_t)nstages * stage_bytes);
+    uint64_t *empty = full + nstages;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t stages = (n + rows_per_stage - 1) / rows_per_stage;
+    const int64_t mine = (int64_t)blockIdx.x < stages ? (stages - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    const size_t row_bytes = (size_t)k * sizeof(T);
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < nstages; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], CW);
+        }
+        fence_barrier_init();
+    }
+    __syncthreads();
+
+    if (warp == CW) {  // ------------------------------------ producer
+        if (lane == 0) {
+            for (int64_t pos = 0; pos < mine; ++pos) {
+                const int slot = (int)(pos % nstages);
+                const int64_t round = pos / nstages;
+                if (round > 0 && !mbar_wait(&empty[slot], (uint32_t)((round - 1) & 1))) break;
+                const int64_t row0 = ((int64_t)blockIdx.x + pos * gridDim.x) * rows_per_stage;
+                const uint32_t bytes = (uint32_t)(min((int64_t)rows_per_stage, n - row0) * (int64_t)row_bytes);
+                mbar_arrive_expect_tx(&full[slot], bytes);
+                bulk_load_1d(smem + (size_t)slot * stage_bytes, w + row0 * k, bytes, &full[slot]);
+            }
+        }
+        return;
+    }
+
+    // Every consumer warp takes the same number of named barriers (one per
+    // row) whatever happens: a warp whose wait fails (an error recorded by any
+    // CTA makes later waits return at once) goes on through its rows without
+    // storing, so no warp is left waiting at a barrier the others skipped.
+    const int chunks = k / 8;
+    int parity = 0;
+    for (int64_t pos = 0; pos < mine; ++pos) {
+        const int slot = (int)(pos % nstages);
+        const bool ok = __all_sync(0xffffffffu, mbar_wait(&full[slot], (uint32_t)((pos / nstages) & 1)));
+        const int64_t row0 = ((int64_t)blockIdx.x + pos * gridDim.x) * rows_per_stage;
+        const int rows = (int)min((int64_t)rows_per_stage, n - row0);
+        for (int rr = 0; rr < rows; ++rr) {
+            const uint4 *row = reinterpret_cast<const uint4 *>(smem + (size_t)slot * stage_bytes + rr * row_bytes);
+            uint32_t mb = 0;
+            for (int c = threadIdx.x; c < chunks; c += CW * 32) {
+                uint32_t x[C::kWords];
+#pragma unroll
+                for (int q = 0; q < VPC; ++q) {
+                    const uint4 t = row[c * VPC + q];
+                    x[4 * q] = t.x, x[4 * q + 1] = t.y, x[4 * q + 2] = t.z, x[4 * q + 3] = t.w;
+                }
+                mb = C::combine(mb, C::absmax(x));
+            }
+            mb = C::fold(mb);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, o));
+            if (lane == 0) red[parity][warp] = mb;
+            asm volatile("bar.sync 1, %0;" ::"r"(CW * 32) : "memory");
+#pragma unroll
+            for (int i = 0; i < CW; ++i) mb = max(mb, red[parity][i]);
+            parity ^= 1;
+            const float s = scale_q<Q>(C::to_f32(mb));
+            const float inv = __frcp_rn(s);
+            const int64_t r = row0 + rr;
+            if (ok && threadIdx.x == 0) scales[r] = s;
+            const bool slow_row = !quot8_exact<true>(s, -1);  // 16-bit weights: one decision per row
+            for (int c = threadIdx.x; c < chunks; c += CW * 32) {
+                uint32_t x[C::kWords];
+#pragma unroll
+                for (int q = 0; q < VPC; ++q) {
+                    const uint4 t = row[c * VPC + q];
+                    x[4 * q] = t.x, x[4 * q + 1] = t.y, x[4 * q + 2] = t.z, x[4 * q + 3] = t.w;
+                }
+                float v[8];
+                float2 q8[4];
+                int allneg = -1;
+                C::unpack(x, v);
+                quot8<C::kCorrected>(v, make_float2(s, s), make_float2(inv, inv), q8, allneg);
+                bool slow = C::kCorrected ? slow_row : !quot8_exact<false>(s, allneg);
+                if (!C::kCorrected) slow = __any_sync(__activemask(), slow);
+                if (BITS == 8) {
+                    const uint2 b = slow ? bytes8_exact(v, s, inv) : bytes8(q8);
+                    if (ok) *reinterpret_cast<uint2 *>(out + r * k + 8 * c) = b;
+                } else {
+                    const uint32_t b = slow ? pack8_exact(v, s, inv) : nibbles8(q8);
+                    if (ok) *reinterpret_cast<uint32_t *>(out + r * (k / 2) + 4 * c) = b;
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
+    }
 }
 
 // Any even group size: one thread per (row, group), scalar loads.
@@ -673,8 +802,48 @@ int grid_for(int64_t units, int threads) {
     return (int)(g < 1 ? 1 : g);
 }
 
+// Streaming per-row launch; OQ_ERR_UNSUPPORTED when the shape or alignment
+// does not qualify (then the two-pass kernel runs).  A stage holds
+// floor(16 KB / row bytes) rows (3 stages), or one row of up to 100 KB (2
+// stages); as many CTAs per SM as shared memory admits, at most 4.
+constexpr int kRowStreamWarps = 8;
+
+template <typename T, int BITS>
+int launch_rowwise_stream(const T *w, int64_t n, int64_t k, uint8_t *out, float *scales, cudaStream_t st,
+                          int nstages = 0, int ctas_per_sm = 0) {
+    if constexpr (std::is_same<T, double>::value) {
+        return OQ_ERR_UNSUPPORTED;
+    } else {
+        const int64_t row_bytes = k * (int64_t)sizeof(T);
+        if (k % 8 != 0 || row_bytes > 100 * 1024 || !aligned(w, 16) || !aligned(out, BITS == 8 ? 8 : 4))
+            return OQ_ERR_UNSUPPORTED;
+        const int rows = (int)std::max<int64_t>(1, std::min<int64_t>(16384 / row_bytes, n));
+        const int stage = (int)(((rows * row_bytes) + 127) / 128 * 128);
+        if (nstages <= 0) nstages = stage <= 16384 ? 3 : 2;
+        const size_t smem = (size_t)nstages * (stage + 16);
+        const void *kern = reinterpret_cast<const void *>(&quant_rowwise_stream_kernel<T, BITS, kRowStreamWarps>);
+        const int threads = (kRowStreamWarps + 1) * 32;
+        const int rc = allow_dynamic_smem(kern, smem);
+        if (rc != OQ_OK) return rc;
+        if (ctas_per_sm <= 0) {
+            OQ_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&ctas_per_sm, kern, threads, smem));
+            ctas_per_sm = std::max(1, std::min(4, ctas_per_sm));
+        }
+        const int64_t grid = std::min<int64_t>(cdiv(n, rows), (int64_t)sm_count() * ctas_per_sm);
+        int ki = (int)k;
+        void *args[] = {(void *)&w, (void *)&n, (void *)&ki, (void *)&rows, (void *)&stage, (void *)&nstages,
+                        (void *)&out, (void *)&scales};
+        OQ_CUDA(cudaLaunchKernel(kern, dim3((unsigned)grid), dim3(threads), args, smem, st));
+        return OQ_OK;
+    }
+}
+
 template <typename T, int BITS>
 int launch_rowwise(const T *w, int64_t n, int64_t k, uint8_t *out, float *scales, cudaStream_t st) {
+    {
+        const int rc = launch_rowwise_stream<T, BITS>(w, n, k, out, scales, st);
+        if (rc != OQ_ERR_UNSUPPORTED) return rc == OQ_OK ? check_launch("quantize (per-row)") : rc;
+    }
     const bool vec = (k % 8 == 0) && aligned(w, 16) && aligned(out, BITS == 8 ? 8 : 4);
     const int64_t units = vec ? k / 8 : k;
     int threads = (int)std::min<int64_t>(kRowThreads, std::max<int64_t>(32, cdiv(units, 32) * 32));
