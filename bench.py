@@ -397,7 +397,7 @@ def measure_bulk_quant(dev, world, rank, peaks, layers=BULK_LAYERS):
 
     lib = nat.load()
     mine = assign_layers(layers, world, rank)
-    pool = [_bulk_layer(dev, layer) for layer in mine[:BULK_POOL]]
+    pool = [_bulk_layer(dev, layer) for layer in mine[:min(BULK_POOL, layers)]]
     flag = torch.zeros(1, dtype=torch.int32, device=dev)
     outs = {}
     for _, n, k in BULK_SHAPES:
@@ -498,7 +498,7 @@ def measure_bulk_quant(dev, world, rank, peaks, layers=BULK_LAYERS):
             "frac": head["frac"],
             "algorithmic_bytes_per_weight": "2 (bf16 read) + 0.5 (packed) + 4/g (scales); INT8: 2 + 1 + 4/K",
         },
-        "config": {"layers": layers, "pool": f"{BULK_POOL} distinct generated layers cycled (6.8 GB > L2)",
+        "config": {"layers": layers, "pool": f"{len(pool)} distinct generated layers cycled ({len(pool) * 1.71:.1f} GB > L2)",
                    "parallelism": f"layers round-robin over {world} GPU(s)",
                    "data": "N(0,0.02) + 0.1% at +-0.2, per-layer seed, generated on the GPU"},
         "gpu_launches": launches,
@@ -605,7 +605,8 @@ def run_ours(args):
 
     args_c = [
         (ctypes.c_void_p(x.data_ptr()), nat.OQ_F16, ctypes.c_void_p(packs[i].data_ptr()),
-         ctypes.c_void_p(scs[i].data_ptr()), ctypes.c_void_p(ys[i].data_ptr()), M, N, K, G, 0, 0)
+         ctypes.c_void_p(scs[i].data_ptr()), ctypes.c_void_p(ys[i].data_ptr()), M, N, K, G, 0,
+         nat.CONFIG_STATIC_WEIGHTS)
         for i in range(COPIES)
     ]
 
@@ -679,7 +680,7 @@ def run_ours(args):
     x_dev = torch.empty_like(x)
     for i in range(min(50, e2e_steps)):
         x_dev.copy_(x_host, non_blocking=True)
-        int4_linear(x_dev, packs[i % COPIES], scs[i % COPIES], N, G, out=ys[i % COPIES])
+        int4_linear(x_dev, packs[i % COPIES], scs[i % COPIES], N, G, out=ys[i % COPIES], static_weights=True)
         y_host.copy_(ys[i % COPIES], non_blocking=True)
         torch.cuda.current_stream().synchronize()
     if world > 1:
@@ -687,7 +688,7 @@ def run_ours(args):
     t0 = time.perf_counter()
     for i in range(e2e_steps):
         x_dev.copy_(x_host, non_blocking=True)
-        int4_linear(x_dev, packs[i % COPIES], scs[i % COPIES], N, G, out=ys[i % COPIES])
+        int4_linear(x_dev, packs[i % COPIES], scs[i % COPIES], N, G, out=ys[i % COPIES], static_weights=True)
         y_host.copy_(ys[i % COPIES], non_blocking=True)
         torch.cuda.current_stream().synchronize()
     e2e_s = time.perf_counter() - t0
@@ -719,7 +720,9 @@ def run_ours(args):
             "m": M, "k": K, "n": N, "group_size": G,
             "weights": f"{COPIES} distinct INT4 copies rotated ({COPIES * ALG_BYTES / 1e6:.0f} MB > L2)",
             "l2": "inputs larger than L2 (weight-copy rotation), no flush",
-            "launch": "CUDA graph of back-to-back launches",
+            "launch": "CUDA graph of back-to-back launches (programmatic dependent launch)",
+            "static_weights": "weights quantized at setup and synchronized, so each launch streams them "
+                              "while the previous one drains (OQ_CONFIG_STATIC_WEIGHTS); x and y stay ordered",
             "parallelism": f"dp{world} (each rank streams its own weight copies)",
         },
         "roofline": {
@@ -751,7 +754,7 @@ def run_ours(args):
         else:
             line["also"] = [measure_sharded_gemm(dev, world, rank, peaks)]
     if not args.no_bulk:
-        line.setdefault("also", []).append(measure_bulk_quant(dev, world, rank, peaks))
+        line.setdefault("also", []).append(measure_bulk_quant(dev, world, rank, peaks, layers=args.bulk_layers))
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline()
     del g_chunk, g_rest
@@ -772,6 +775,8 @@ def main(argv=None):
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gemm", action="store_true", help="skip the M=2048 prefill GEMM measurement")
     ap.add_argument("--no-bulk", action="store_true", help="skip the bulk-quantization (70B stack) measurement")
+    ap.add_argument("--bulk-layers", type=int, default=BULK_LAYERS,
+                    help="layers of the bulk-quantization stack (default 80; fewer for profiling)")
     args = ap.parse_args(argv)
     if args.steps < 1 or args.warmup < 0:
         ap.error("steps must be >= 1 and warmup >= 0")

@@ -72,6 +72,15 @@ typedef void *oq_stream_t; /* a cudaStream_t */
  * of it, and ~2.5x fewer instructions per weight. */
 #define OQ_CONFIG_EXACT_ROUNDING 16
 
+/* oq_int4_linear `config` flag: the packed weights and scales are static --
+ * written before any kernel still in flight on `stream` (e.g. quantized at
+ * load time, then synchronized).  The GEMV then streams them while the
+ * previous kernel in the stream drains (programmatic dependent launch)
+ * instead of after it; x and y are still ordered after that kernel.  Without
+ * the flag the GEMV reads nothing before the previous kernel has finished.
+ * No counterpart in the reference (its Triton launch is stream-ordered). */
+#define OQ_CONFIG_STATIC_WEIGHTS 32
+
 /* Library version string ("openquant_b200 <x.y.z> sm_100a"). */
 OQ_API const char *oq_version(void);
 
@@ -177,9 +186,10 @@ OQ_API int oq_dequant_int4_group(const uint8_t *packed, const float *scales,
  *             SM) = (8,4,2) (16,2,2) (12,2,2) (16,1,2) (8,2,3) (8,2,4)
  *             (8,4,4), and 8, 9, 10 the TMA-fed kernel with 8 or 16
  *             consumer warps and one CTA per SM, or 8 warps and two CTAs per
- *             SM (M <= 16) -- only the fp32 summation order changes;
- *             `openquant tune` picks it.  | OQ_CONFIG_EXACT_ROUNDING: see
- *             above.
+ *             SM (M <= 16), 12 one CTA per 16-row tile with four CTAs per SM
+ *             (M <= 16, K <= 4096) -- only the fp32 summation order changes;
+ *             `openquant tune` picks it.  | OQ_CONFIG_EXACT_ROUNDING,
+ *             | OQ_CONFIG_STATIC_WEIGHTS: see above.
  */
 OQ_API int oq_int4_linear(const void *x, int x_dtype, const uint8_t *packed,
                    const float *scales, float *y, int64_t m, int64_t n,

@@ -163,7 +163,7 @@ __global__ void __launch_bounds__(WARPS * 32, MINB) gemv_int4_kernel(const XT *_
                                                                const uint8_t *__restrict__ packed,
                                                                const float *__restrict__ scales,
                                                                float *__restrict__ y, int m, int n, int k, int kp,
-                                                               int gshift, int xstride) {
+                                                               int gshift, int xstride, int prefetch) {
     static_assert(!SA || std::is_same<XT, __half>::value, "scale-after mode is for fp16 x");
     // Dynamic shared memory: the double-buffered cross-warp reduction, then
     // the staged x.
@@ -217,14 +217,18 @@ __global__ void __launch_bounds__(WARPS * 32, MINB) gemv_int4_kernel(const XT *_
             r_jj = cpw - 1;  // stay on the last position
         }
     };
+    // Dependent launches may start now; they wait for this grid before
+    // touching anything it writes.  Weights are read before this grid's own
+    // wait only with `prefetch` (static weights: written before any kernel
+    // still in flight on the stream).
+    asm volatile("griddepcontrol.launch_dependents;");
+    if (!prefetch) asm volatile("griddepcontrol.wait;" ::: "memory");
     if (npos > 0) {
         set_rows(0);
 #pragma unroll
         for (int u = 0; u < U; ++u) load(u);
     }
-
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-    asm volatile("griddepcontrol.launch_dependents;");
+    if (prefetch) asm volatile("griddepcontrol.wait;" ::: "memory");
     if (npos == 0) return;
 
     if (XS) {  // x [m][k] -> xs [m][xstride] halves, zero beyond k
@@ -333,8 +337,11 @@ __global__ void __launch_bounds__(WARPS * 32, MINB) gemv_int4_kernel(const XT *_
 // empty[slot].  At the end of a tile the consumer warps reduce their partial
 // sums in a fixed order (named barrier 1, producer excluded).
 //
-// Everything the producer streams is read-only, so it starts before
-// griddepcontrol.wait; the consumers read x and write y after it.
+// PDL: every CTA lets dependent launches start at once.  The consumers read
+// x and write y after griddepcontrol.wait; the producer streams the weights
+// and scales after it too, unless the caller declared them static
+// (`prefetch`: written before any kernel still in flight on the stream), in
+// which case they stream while the previous grid drains.
 template <int CW, int CPW>
 struct TmaGemvLayout {
     static constexpr int kStageCols = 128 * CW * CPW;  // columns per stage
@@ -346,7 +353,7 @@ template <typename XT, int NT, int CW, int CPW, bool SA, bool XS, bool STMA>
 __global__ void __launch_bounds__((CW + 1) * 32, CW <= 8 ? 2 : 1)
     gemv_tma_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap smap,
                     const XT *__restrict__ x, const float *__restrict__ scales, float *__restrict__ y, int m, int n,
-                    int k, int kp, int gshift, int xstride, int nstages) {
+                    int k, int kp, int gshift, int xstride, int nstages, int prefetch) {
     static_assert(!SA || std::is_same<XT, __half>::value, "scale-after mode is for fp16 x");
     using L = TmaGemvLayout<CW, CPW>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -369,6 +376,9 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW <= 8 ? 2 : 1)
     const int spt = (kp + L::kStageCols - 1) / L::kStageCols;  // stages per tile
     const int npos = my_tiles * spt;
 
+    // Dependent launches may start now; they wait for this grid before
+    // touching anything it writes (as in the ring kernel).
+    asm volatile("griddepcontrol.launch_dependents;");
     if (threadIdx.x == 0) {
         for (int i = 0; i < nstages; ++i) {
             mbar_init(&full[i], 1);   // the producer's expect_tx arrival
@@ -382,6 +392,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW <= 8 ? 2 : 1)
         if (lane == 0) {
             tma_prefetch_desc(&wmap);
             if (STMA) tma_prefetch_desc(&smap);
+            if (!prefetch) asm volatile("griddepcontrol.wait;" ::: "memory");
             for (int pos = 0; pos < npos; ++pos) {
                 const int slot = pos % nstages, round = pos / nstages;
                 if (round > 0 && !mbar_wait(&empty[slot], (round - 1) & 1)) break;
@@ -404,7 +415,6 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW <= 8 ? 2 : 1)
     // ------------------------------------------------------ consumers
     const int gi = lane >> 2, t = lane & 3;
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    asm volatile("griddepcontrol.launch_dependents;");
     if (XS) {  // x [m][k] -> xs [m][xstride], zero beyond k (SA: pair-permuted)
         const int rowv = xstride / 8, kv = k / 8;
         for (int i = threadIdx.x; i < m * rowv; i += CW * 32) {
@@ -524,6 +534,151 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW <= 8 ? 2 : 1)
     }
 }
 
+// ----------------------------------------------------------- tile GEMV ----
+//
+// Small decode layers (KP <= 4096, one 16-row tile per CTA): 8 warps and no
+// producer warp, up to four CTAs per SM -- two of this launch and two of the
+// next, which then streams its tile (static weights) while this one
+// computes.  Thread 0 issues the tile's TMA boxes (the 32 KB stage and the
+// scale box of gemv_tma_kernel) at entry; after griddepcontrol.wait every
+// warp takes chunks w, w + 8, ... exactly as gemv_tma_kernel's consumers do
+// and the partial sums are reduced in the same fixed order, so both kernels
+// give identical results.
+template <typename XT, int NT, bool SA, bool XS, bool STMA>
+__global__ void __launch_bounds__(256, 4)
+    gemv_tile_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap smap,
+                     const XT *__restrict__ x, const float *__restrict__ scales, float *__restrict__ y, int m, int n,
+                     int k, int kp, int gshift, int xstride, int prefetch) {
+    static_assert(!SA || std::is_same<XT, __half>::value, "scale-after mode is for fp16 x");
+    constexpr int CW = 8, CPW = 4;
+    using L = TmaGemvLayout<CW, CPW>;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+    const int spr = L::kStageCols >> gshift;  // scales per row in the stage
+    const int sbytes = ((16 * spr * 4 + 127) / 128) * 128;
+    const uint8_t *wst = smem;                                               // [boxes][16][128]
+    float *sst = reinterpret_cast<float *>(smem + L::kStageBytes);           // [16][spr]
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + L::kStageBytes + sbytes);
+    auto red = reinterpret_cast<float(*)[NT][4][32]>(full + 2);              // [CW]
+    XT *xs = reinterpret_cast<XT *>(reinterpret_cast<uint8_t *>(red) + gemv_red_bytes(CW, NT) / 2);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int gi = lane >> 2, t = lane & 3;
+    const int groups = kp >> gshift;
+    const int nchunks = (kp + 127) >> 7;
+    const int row0 = (int)blockIdx.x * 16;
+
+    // Dependent launches may start now; they wait for this grid before
+    // touching anything it writes.
+    asm volatile("griddepcontrol.launch_dependents;");
+    if (threadIdx.x == 0) {
+        mbar_init(&full[0], 1);
+        fence_barrier_init();
+        tma_prefetch_desc(&wmap);
+        if (STMA) tma_prefetch_desc(&smap);
+        if (!prefetch) asm volatile("griddepcontrol.wait;" ::: "memory");
+        mbar_arrive_expect_tx(&full[0], L::kStageBytes + (STMA ? 16 * spr * 4 : 0));
+#pragma unroll
+        for (int b = 0; b < L::kBoxes; ++b)
+            tma_load_2d(smem + b * 2048, &wmap, &full[0], 128 * b, row0);
+        if (STMA) tma_load_2d(sst, &smap, &full[0], 0, row0);
+    }
+
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (XS) {  // x [m][k] -> xs [m][xstride], zero beyond k (SA: pair-permuted)
+        const int rowv = xstride / 8, kv = k / 8;
+        for (int i = threadIdx.x; i < m * rowv; i += CW * 32) {
+            const int r = i / rowv, c = i - r * rowv;
+            uint4 v = c < kv ? __ldg(reinterpret_cast<const uint4 *>(x) + (size_t)r * kv + c) : make_uint4(0, 0, 0, 0);
+            if (SA)
+                v = make_uint4(__byte_perm(v.x, v.z, 0x5410), __byte_perm(v.y, v.w, 0x5410),
+                               __byte_perm(v.x, v.z, 0x7632), __byte_perm(v.y, v.w, 0x7632));
+            reinterpret_cast<uint4 *>(xs)[i] = v;
+        }
+    }
+    __syncthreads();  // xs staged; full[0] initialised before anyone waits on it
+    uint32_t xaddr[NT];
+    bool xon[NT];
+    const XT *xg[NT];
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+        const int mb = 8 * j + gi;
+        xon[j] = mb < m;
+        const int mr = xon[j] ? mb : 0;
+        xaddr[j] = smem_u32(xs) + (uint32_t)(mr * xstride + 32 * t) * 2u;
+        xg[j] = x + (size_t)mr * k + 32 * t;
+    }
+    uint4 xb[NT];
+#pragma unroll
+    for (int j = 0; j < NT; ++j) xb[j] = make_uint4(0, 0, 0, 0);
+    float acc[2][NT][4];
+#pragma unroll
+    for (int a = 0; a < 2; ++a)
+#pragma unroll
+        for (int j = 0; j < NT; ++j) acc[a][j][0] = acc[a][j][1] = acc[a][j][2] = acc[a][j][3] = 0.0f;
+
+    float sreg[CPW][2];
+    if (!STMA) {  // scales straight from global memory (row pitch not 16-byte aligned)
+        const int ra = min(row0 + gi, n - 1), rb = min(row0 + gi + 8, n - 1);
+#pragma unroll
+        for (int q = 0; q < CPW; ++q) {
+            const int c = warp + q * CW;
+            const int col = min((128 * c + 32 * t) >> gshift, groups - 1);
+            sreg[q][0] = __ldg(scales + (size_t)ra * groups + col);
+            sreg[q][1] = __ldg(scales + (size_t)rb * groups + col);
+        }
+    }
+    const bool ok = mbar_wait(&full[0], 0);
+    if (ok) {
+        auto do_chunk = [&](int q) {
+            const int c = warp + q * CW;  // chunk within the row (the stage is the whole row)
+            const uint32_t piece = (uint32_t)(c >> 1) * 2048u + (uint32_t)gi * 128u +
+                                   (uint32_t)(((((c & 1) << 2) + t) ^ (gi & 7)) << 4);
+            const uint4 wa = *reinterpret_cast<const uint4 *>(wst + piece);
+            const uint4 wb = *reinterpret_cast<const uint4 *>(wst + piece + 8 * 128);
+            const int scol = (c * 128 + 32 * t) >> gshift;
+            const float sa = STMA ? sst[gi * spr + scol] : sreg[q][0];
+            const float sb = STMA ? sst[(gi + 8) * spr + scol] : sreg[q][1];
+            const bool in = 128 * c + 32 * t < kp;
+            const uint32_t qa[4] = {wa.x, wa.y, wa.z, wa.w};
+            const uint32_t qb[4] = {wb.x, wb.y, wb.z, wb.w};
+            if constexpr (SA) {
+                gemv_chunk_sa<NT, XS>(c, qa, qb, in ? sa : 0.0f, in ? sb : 0.0f, xaddr, xon, xg, xb, acc);
+            } else {
+                const DqScale dsa = make_dq_scale(in ? sa : 0.0f), dsb = make_dq_scale(in ? sb : 0.0f);
+                if (__all_sync(0xffffffffu, dsa.fast && dsb.fast))
+                    gemv_chunk<XT, NT, XS, true>(c, qa, qb, dsa, dsb, xaddr, xon, xg, xb, acc);
+                else
+                    gemv_chunk<XT, NT, XS, false>(c, qa, qb, dsa, dsb, xaddr, xon, xg, xb, acc);
+            }
+        };
+        if ((CPW - 1) * CW + warp < nchunks) {
+#pragma unroll
+            for (int q = 0; q < CPW; ++q) do_chunk(q);
+        } else {
+#pragma unroll
+            for (int q = 0; q < CPW; ++q)
+                if (warp + q * CW < nchunks) do_chunk(q);
+        }
+    }
+    // Fixed-order reduction over the warps, as in gemv_tma_kernel.
+#pragma unroll
+    for (int j = 0; j < NT; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) red[warp][j][e][lane] = acc[0][j][e] + acc[1][j][e];
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < NT * 4 * 32; idx += CW * 32) {
+        const int j = idx / 128, e = (idx / 32) % 4, ln = idx % 32;
+        float v = 0.0f;
+#pragma unroll
+        for (int wv = 0; wv < CW; ++wv) v += red[wv][j][e][ln];
+        const int g2 = ln >> 2, t2 = ln & 3;
+        const int row = row0 + g2 + (e >= 2 ? 8 : 0);
+        const int mb = 8 * j + 2 * t2 + (e & 1);
+        if (ok && row < n && mb < m) y[(size_t)mb * n + row] = v;
+    }
+}
+
 // ------------------------------------------------------------- SIMT ----
 //
 // Any shape and any even group size: one warp per weight row, lanes stride
@@ -586,14 +741,14 @@ inline int allow_max_smem(const void *kern) {
     return OQ_OK;
 }
 
-// Launch with programmatic stream serialization: a GEMV that follows
-// another kernel in the stream may start (and prefetch its weights) while
-// that kernel drains.  Without a preceding PDL-aware kernel it behaves like a
-// normal launch.
+// Launch with programmatic stream serialization: a GEMV that follows a
+// PDL-triggering kernel in the stream may start while that kernel drains
+// (and, with `prefetch`, stream its static weights meanwhile).  After any
+// other kernel it behaves like a normal launch.
 template <typename Kern, typename XT>
 int launch_pdl(Kern kern, unsigned blocks, unsigned threads, size_t smem, cudaStream_t st, const XT *x,
                const uint8_t *packed, const float *scales, float *y, int m, int n, int k, int kp, int gshift,
-               int xstride) {
+               int xstride, int prefetch) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(blocks);
     cfg.blockDim = dim3(threads);
@@ -604,7 +759,7 @@ int launch_pdl(Kern kern, unsigned blocks, unsigned threads, size_t smem, cudaSt
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t err = cudaLaunchKernelEx(&cfg, kern, x, packed, scales, y, m, n, k, kp, gshift, xstride);
+    cudaError_t err = cudaLaunchKernelEx(&cfg, kern, x, packed, scales, y, m, n, k, kp, gshift, xstride, prefetch);
     if (err != cudaSuccess) {
         set_error("int4_linear (GEMV): launch failed: %s", cudaGetErrorString(err));
         return OQ_ERR_CUDA;
@@ -623,7 +778,7 @@ inline size_t gemv_xs_bytes(int64_t m, int64_t kp, int xsize) {
 
 template <typename XT, int NT, int WARPS, int U, int MINB, bool SA>
 int launch_gemv_t(const XT *x, const uint8_t *packed, const float *scales, float *y, int64_t m, int64_t n,
-                  int64_t k, int64_t kp, int gshift, cudaStream_t st) {
+                  int64_t k, int64_t kp, int gshift, int prefetch, cudaStream_t st) {
     // Persistent grid: MINB CTAs per SM, each looping over 16-row tiles.
     const int64_t tiles = cdiv(n, 16);
     const unsigned blocks = (unsigned)std::min<int64_t>(tiles, (int64_t)sm_count() * MINB);
@@ -635,7 +790,7 @@ int launch_gemv_t(const XT *x, const uint8_t *packed, const float *scales, float
     const int rc = allow_max_smem(reinterpret_cast<const void *>(kern));
     if (rc != OQ_OK) return rc;
     return launch_pdl(kern, blocks, WARPS * 32, smem, st, x, packed, scales, y, (int)m, (int)n, (int)k, (int)kp,
-                      gshift, xstride);
+                      gshift, xstride, prefetch);
 }
 
 // Stage count and shared-memory bytes of the TMA GEMV, or 0 stages when the
@@ -666,9 +821,32 @@ inline int tma_gemv_plan(int64_t m, int64_t k, int64_t kp, int g, int nt, int xs
     return stages;
 }
 
+// Tensor maps of the TMA GEMVs: the packed rows in 16-row x 128-byte boxes
+// (128-byte swizzle) and, when the scale row pitch is a multiple of 16 bytes,
+// the scales in 16-row boxes of one stage's groups (*stma = true).
+template <int CW, int CPW>
+int make_gemv_maps(const uint8_t *packed, const float *scales, int64_t n, int64_t kp, int g, CUtensorMap *wmap,
+                   CUtensorMap *smap, bool *stma) {
+    using L = TmaGemvLayout<CW, CPW>;
+    int rc = make_tensor_map_2d(wmap, packed, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)(kp / 2), (uint64_t)n,
+                                (uint64_t)(kp / 2), 128, 16, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != OQ_OK) return rc;
+    const int64_t groups = kp / g;
+    *stma = (groups * 4) % 16 == 0 && aligned(scales, 16) && (L::kStageCols / g) * 4 % 16 == 0;
+    if (*stma) {
+        rc = make_tensor_map_2d(smap, scales, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)groups, (uint64_t)n,
+                                (uint64_t)(groups * 4), (uint32_t)(L::kStageCols / g), 16,
+                                CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (rc != OQ_OK) return rc;
+    } else {
+        *smap = *wmap;  // unused
+    }
+    return OQ_OK;
+}
+
 template <typename XT, int NT, int CW, int CPW, bool SA, int CTAS = 1>
 int launch_gemv_tma(const XT *x, const uint8_t *packed, const float *scales, float *y, int64_t m, int64_t n,
-                    int64_t k, int64_t kp, int g, int gshift, cudaStream_t st) {
+                    int64_t k, int64_t kp, int g, int gshift, int prefetch, cudaStream_t st) {
     using L = TmaGemvLayout<CW, CPW>;
     size_t smem = 0;
     int xstride = 0;
@@ -679,19 +857,9 @@ int launch_gemv_tma(const XT *x, const uint8_t *packed, const float *scales, flo
     const int stages = tma_gemv_plan<CW, CPW>(m, k, kp, g, NT, (int)sizeof(XT), &smem, &xstride, &xs, CTAS, max_pos);
     if (stages == 0) return invalid("TMA GEMV: shape does not fit in shared memory");
     CUtensorMap wmap, smap;
-    int rc = make_tensor_map_2d(&wmap, packed, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)(kp / 2), (uint64_t)n,
-                                (uint64_t)(kp / 2), 128, 16, CU_TENSOR_MAP_SWIZZLE_128B);
+    bool stma = false;
+    const int rc = make_gemv_maps<CW, CPW>(packed, scales, n, kp, g, &wmap, &smap, &stma);
     if (rc != OQ_OK) return rc;
-    const int64_t groups = kp / g;
-    const bool stma = (groups * 4) % 16 == 0 && aligned(scales, 16) && (L::kStageCols / g) * 4 % 16 == 0;
-    if (stma) {
-        rc = make_tensor_map_2d(&smap, scales, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)groups, (uint64_t)n,
-                                (uint64_t)(groups * 4), (uint32_t)(L::kStageCols / g), 16,
-                                CU_TENSOR_MAP_SWIZZLE_NONE);
-        if (rc != OQ_OK) return rc;
-    } else {
-        smap = wmap;  // unused
-    }
     auto pick = [&](auto kern) -> int {
         int rc2 = allow_max_smem(reinterpret_cast<const void *>(kern));
         if (rc2 != OQ_OK) return rc2;
@@ -706,7 +874,7 @@ int launch_gemv_tma(const XT *x, const uint8_t *packed, const float *scales, flo
         cfg.attrs = attr;
         cfg.numAttrs = 1;
         cudaError_t err = cudaLaunchKernelEx(&cfg, kern, wmap, smap, x, scales, y, (int)m, (int)n, (int)k, (int)kp,
-                                             gshift, xstride, stages);
+                                             gshift, xstride, stages, prefetch);
         if (err != cudaSuccess) {
             set_error("int4_linear (TMA GEMV): launch failed: %s", cudaGetErrorString(err));
             return OQ_ERR_CUDA;
@@ -718,6 +886,57 @@ int launch_gemv_tma(const XT *x, const uint8_t *packed, const float *scales, flo
                     : pick(gemv_tma_kernel<XT, NT, CW, CPW, SA, true, false>);
     return stma ? pick(gemv_tma_kernel<XT, NT, CW, CPW, SA, false, true>)
                 : pick(gemv_tma_kernel<XT, NT, CW, CPW, SA, false, false>);
+}
+
+// Tile GEMV (config 12): x staged in shared memory up to this size, else read
+// from global memory (needs KP == K, whole 128-column chunks).
+constexpr int64_t kTileXs = 16 * 1024;
+
+inline bool gemv_tile_ok(int64_t m, int64_t n, int64_t k, int64_t kp, int g, const uint8_t *packed) {
+    const int64_t xstride = cdiv(kp, 128) * 128 + 8;
+    const bool xs = m * xstride * 2 <= kTileXs;
+    return m <= 16 && g >= 32 && g <= 4096 && kp <= 4096 && aligned(packed, 16) && (kp / 2) % 16 == 0 &&
+           n < (1ll << 31) && (xs || (kp == k && kp % 128 == 0));
+}
+
+template <typename XT, int NT, bool SA>
+int launch_gemv_tile(const XT *x, const uint8_t *packed, const float *scales, float *y, int64_t m, int64_t n,
+                     int64_t k, int64_t kp, int g, int gshift, int prefetch, cudaStream_t st) {
+    using L = TmaGemvLayout<8, 4>;
+    if (!gemv_tile_ok(m, n, k, kp, g, packed)) return invalid("tile GEMV (config 12) does not take this shape");
+    const int64_t xstride = cdiv(kp, 128) * 128 + 8;
+    const size_t xbytes = (size_t)(m * xstride) * sizeof(XT);
+    const bool xs = (int64_t)xbytes <= kTileXs;
+    const size_t sbytes = (size_t)cdiv(16 * (L::kStageCols / g) * 4, 128) * 128;
+    const size_t smem = 1024 + L::kStageBytes + sbytes + 16 + gemv_red_bytes(8, NT) / 2 + (xs ? xbytes : 0);
+    CUtensorMap wmap, smap;
+    bool stma = false;
+    int rc = make_gemv_maps<8, 4>(packed, scales, n, kp, g, &wmap, &smap, &stma);
+    if (rc != OQ_OK) return rc;
+    auto pick = [&](auto kern) -> int {
+        int rc2 = allow_dynamic_smem(reinterpret_cast<const void *>(kern), smem);
+        if (rc2 != OQ_OK) return rc2;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)cdiv(n, 16));
+        cfg.blockDim = dim3(256);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        cudaError_t err = cudaLaunchKernelEx(&cfg, kern, wmap, smap, x, scales, y, (int)m, (int)n, (int)k, (int)kp,
+                                             gshift, (int)xstride, prefetch);
+        if (err != cudaSuccess) {
+            set_error("int4_linear (tile GEMV): launch failed: %s", cudaGetErrorString(err));
+            return OQ_ERR_CUDA;
+        }
+        return OQ_OK;
+    };
+    if (xs)
+        return stma ? pick(gemv_tile_kernel<XT, NT, SA, true, true>) : pick(gemv_tile_kernel<XT, NT, SA, true, false>);
+    return stma ? pick(gemv_tile_kernel<XT, NT, SA, false, true>) : pick(gemv_tile_kernel<XT, NT, SA, false, false>);
 }
 
 // True when the TMA GEMV takes this shape (M <= 16, 32 <= g <= the stage
@@ -739,43 +958,51 @@ bool tma_gemv_ok(int64_t m, int64_t k, int64_t kp, int g, const uint8_t *packed)
 //   8, 9  TMA-fed persistent kernel with 8 / 16 consumer warps, 32 KB
 //         stages (M <= 16)
 //   10    TMA-fed, 8 consumer warps, two CTAs per SM with the stage ring
-//         sized to the CTA's work, so consecutive launches overlap (PDL)
+//         sized to the CTA's work
+//   12    one CTA of 8 warps per 16-row tile, no producer warp, four CTAs
+//         per SM (KP <= 4096, M <= 16): the next launch's CTAs fit beside
+//         this one's, so back-to-back GEMVs overlap (PDL)
 // config & 16 (OQ_CONFIG_EXACT_ROUNDING) forces the exact weight rounding
 // for fp16 x, which otherwise uses the scale-after path when g % 128 == 0.
-constexpr int kGemvConfigs = 10;
+// config & 32 (OQ_CONFIG_STATIC_WEIGHTS) lets the weights and scales stream
+// before the wait on the previous kernel in the stream.
+constexpr int kGemvConfigs = 12;
 
 template <typename XT, int NT, bool SA>
 int launch_gemv_nt(int config, const XT *x, const uint8_t *packed, const float *scales, float *y, int64_t m,
-                   int64_t n, int64_t k, int64_t kp, int g, int gshift, cudaStream_t st) {
+                   int64_t n, int64_t k, int64_t kp, int g, int gshift, int pf, cudaStream_t st) {
     switch (config) {
-        case 1: return launch_gemv_t<XT, NT, 8, 4, 2, SA>(x, packed, scales, y, m, n, k, kp, gshift, st);
-        case 2: return launch_gemv_t<XT, NT, 16, 2, 2, SA>(x, packed, scales, y, m, n, k, kp, gshift, st);
-        case 3: return launch_gemv_t<XT, NT, 12, 2, 2, SA>(x, packed, scales, y, m, n, k, kp, gshift, st);
-        case 4: return launch_gemv_t<XT, NT, 16, 1, 2, SA>(x, packed, scales, y, m, n, k, kp, gshift, st);
-        case 6: return launch_gemv_t<XT, NT, 8, 2, 4, SA>(x, packed, scales, y, m, n, k, kp, gshift, st);
-        case 7: return launch_gemv_t<XT, NT, 8, 4, 4, SA>(x, packed, scales, y, m, n, k, kp, gshift, st);
+        case 1: return launch_gemv_t<XT, NT, 8, 4, 2, SA>(x, packed, scales, y, m, n, k, kp, gshift, pf, st);
+        case 2: return launch_gemv_t<XT, NT, 16, 2, 2, SA>(x, packed, scales, y, m, n, k, kp, gshift, pf, st);
+        case 3: return launch_gemv_t<XT, NT, 12, 2, 2, SA>(x, packed, scales, y, m, n, k, kp, gshift, pf, st);
+        case 4: return launch_gemv_t<XT, NT, 16, 1, 2, SA>(x, packed, scales, y, m, n, k, kp, gshift, pf, st);
+        case 6: return launch_gemv_t<XT, NT, 8, 2, 4, SA>(x, packed, scales, y, m, n, k, kp, gshift, pf, st);
+        case 7: return launch_gemv_t<XT, NT, 8, 4, 4, SA>(x, packed, scales, y, m, n, k, kp, gshift, pf, st);
         case 8:
-            if constexpr (NT <= 2) return launch_gemv_tma<XT, NT, 8, 4, SA>(x, packed, scales, y, m, n, k, kp, g, gshift, st);
+            if constexpr (NT <= 2) return launch_gemv_tma<XT, NT, 8, 4, SA>(x, packed, scales, y, m, n, k, kp, g, gshift, pf, st);
             return invalid("TMA GEMV needs M <= 16");
         case 9:
-            if constexpr (NT <= 2) return launch_gemv_tma<XT, NT, 16, 2, SA>(x, packed, scales, y, m, n, k, kp, g, gshift, st);
+            if constexpr (NT <= 2) return launch_gemv_tma<XT, NT, 16, 2, SA>(x, packed, scales, y, m, n, k, kp, g, gshift, pf, st);
             return invalid("TMA GEMV needs M <= 16");
         case 10:
             if constexpr (NT <= 2)
-                return launch_gemv_tma<XT, NT, 8, 4, SA, 2>(x, packed, scales, y, m, n, k, kp, g, gshift, st);
+                return launch_gemv_tma<XT, NT, 8, 4, SA, 2>(x, packed, scales, y, m, n, k, kp, g, gshift, pf, st);
             return invalid("TMA GEMV needs M <= 16");
-        default: return launch_gemv_t<XT, NT, 8, 2, 3, SA>(x, packed, scales, y, m, n, k, kp, gshift, st);
+        case 12:
+            if constexpr (NT <= 2) return launch_gemv_tile<XT, NT, SA>(x, packed, scales, y, m, n, k, kp, g, gshift, pf, st);
+            return invalid("tile GEMV needs M <= 16");
+        default: return launch_gemv_t<XT, NT, 8, 2, 3, SA>(x, packed, scales, y, m, n, k, kp, gshift, pf, st);
     }
 }
 
 template <typename XT, bool SA>
 int launch_gemv_sa(int shape, const XT *x, const uint8_t *packed, const float *scales, float *y, int64_t m,
-                   int64_t n, int64_t k, int64_t kp, int g, int gshift, cudaStream_t st) {
+                   int64_t n, int64_t k, int64_t kp, int g, int gshift, int pf, cudaStream_t st) {
     switch ((m + 7) / 8) {
-        case 1: return launch_gemv_nt<XT, 1, SA>(shape, x, packed, scales, y, m, n, k, kp, g, gshift, st);
-        case 2: return launch_gemv_nt<XT, 2, SA>(shape, x, packed, scales, y, m, n, k, kp, g, gshift, st);
-        case 3: case 4: return launch_gemv_nt<XT, 4, SA>(shape, x, packed, scales, y, m, n, k, kp, g, gshift, st);
-        default: return launch_gemv_t<XT, 8, 8, 2, 1, SA>(x, packed, scales, y, m, n, k, kp, gshift, st);
+        case 1: return launch_gemv_nt<XT, 1, SA>(shape, x, packed, scales, y, m, n, k, kp, g, gshift, pf, st);
+        case 2: return launch_gemv_nt<XT, 2, SA>(shape, x, packed, scales, y, m, n, k, kp, g, gshift, pf, st);
+        case 3: case 4: return launch_gemv_nt<XT, 4, SA>(shape, x, packed, scales, y, m, n, k, kp, g, gshift, pf, st);
+        default: return launch_gemv_t<XT, 8, 8, 2, 1, SA>(x, packed, scales, y, m, n, k, kp, gshift, pf, st);
     }
 }
 
@@ -800,14 +1027,16 @@ int launch_gemv(const XT *x, const uint8_t *packed, const float *scales, float *
     if ((shape == 8 && !tma_gemv_ok<8, 4>(m, k, kp, g, packed)) || (shape == 9 && !tma_gemv_ok<16, 2>(m, k, kp, g, packed)) ||
         (shape == 10 && !tma_gemv_ok<8, 4, 2>(m, k, kp, g, packed)))
         return invalid("TMA GEMV (config %d) does not take this shape", shape);
+    if (shape == 11) return invalid("GEMV config 11 is not a launch shape");
     // Scale-after pays off for M <= 8; with two n-tiles its extra partial
     // sums cost more registers than the exact path saves.
     const bool exact = (config & OQ_CONFIG_EXACT_ROUNDING) != 0 || (auto_shape && nt > 1);
+    const int pf = (config & OQ_CONFIG_STATIC_WEIGHTS) != 0;
     if constexpr (std::is_same<XT, __half>::value) {
         if (!exact && g % 128 == 0)
-            return launch_gemv_sa<XT, true>(shape, x, packed, scales, y, m, n, k, kp, g, gshift, st);
+            return launch_gemv_sa<XT, true>(shape, x, packed, scales, y, m, n, k, kp, g, gshift, pf, st);
     }
-    return launch_gemv_sa<XT, false>(shape, x, packed, scales, y, m, n, k, kp, g, gshift, st);
+    return launch_gemv_sa<XT, false>(shape, x, packed, scales, y, m, n, k, kp, g, gshift, pf, st);
 }
 
 template <typename XT>

@@ -18,7 +18,7 @@ __all__ = ["int4_linear"]
 
 
 def int4_linear(x, packed, scales, out_features, group_size, *, block_m=64, block_n=64, block_k=64, num_warps=4,
-                kernel=None, out=None, exact_rounding=False):
+                kernel=None, out=None, exact_rounding=False, static_weights=False):
     """y = x @ W^T in fp32, W[n, k] = round_x(int4(n, k) * scales[n, k // g]).
 
     Arguments and errors follow triton_int4.py:78-118 (ValueError for each
@@ -39,6 +39,11 @@ def int4_linear(x, packed, scales, out_features, group_size, *, block_m=64, bloc
     reference, and within the parity tolerance of it).  exact_rounding=True
     instead rounds every weight to fp16 as the reference kernel does, bit
     for bit; bf16 x and larger M always do.
+
+    static_weights=True declares that `packed` and `scales` were written
+    before any kernel still in flight on the stream (quantized at load time
+    and synchronized): the decode GEMV then streams them while the previous
+    kernel drains instead of after it.  Results are unchanged.
     """
     if x.ndim != 2 or x.dtype not in (torch.float16, torch.bfloat16):
         raise ValueError("Input must be a 2D FP16 tensor")
@@ -86,6 +91,8 @@ def int4_linear(x, packed, scales, out_features, group_size, *, block_m=64, bloc
         sel, split = nat.KERNELS[kernel], 0
     if exact_rounding:
         split |= nat.CONFIG_EXACT_ROUNDING
+    if static_weights:
+        split |= nat.CONFIG_STATIC_WEIGHTS
     code = nat.OQ_F16 if x.dtype == torch.float16 else nat.OQ_BF16
     with torch.cuda.device(x.device):
         nat.check(nat.load().oq_int4_linear(nat.ptr(x), code, nat.ptr(packed), nat.ptr(scales), nat.ptr(out),
