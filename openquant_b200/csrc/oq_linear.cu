@@ -74,9 +74,12 @@ __host__ __device__ constexpr size_t gemv_red_bytes(int warps, int nt) { return 
 // (1024 + 16 u1, 1024 + 16 u5), and W >> 8 the same for nibbles 2, 6 and 3,
 // 7.  One HSUB2 of 1032 (or 1024 + 128) leaves q (or 16 q) exactly.  The
 // "class 0" k16 step takes nibbles {0,4,2,6}, the "class 1" step nibbles
-// {1,5,3,7} (16 q); x is staged in the matching order, so one 16-byte load
-// gives both steps' B fragments.  Products of fp16 q and x are exact and the
-// tensor core sums them in fp32; y += s * (sum0 + sum1 / 16) per chunk.
+// {1,5,3,7} (16 q); x is staged in the matching order with the class-1
+// halves divided by 16 (sa_perm_x), so one 16-byte load gives both steps' B
+// fragments and both steps accumulate q * x into the same fp32 sums.
+// Products of fp16 q and x are exact (x / 16 too, unless it falls below the
+// fp16 normal range, |x| < 2^-10) and the tensor core sums them in fp32;
+// y += s * sum per chunk.
 __device__ __forceinline__ uint32_t lop3_and_xor(uint32_t a, uint32_t b, uint32_t c) {
     uint32_t d;
     asm("lop3.b32 %0, %1, %2, %3, 0x6A;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
@@ -88,14 +91,25 @@ __device__ __forceinline__ uint32_t hsub2_u32(uint32_t a, uint32_t b) {
     return *reinterpret_cast<uint32_t *>(&r);
 }
 
+// Eight fp16 x values in natural order -> the scale-after layout:
+// (x0, x4) (x2, x6) for the class-0 step, (x1, x5)/16 (x3, x7)/16 for the
+// class-1 step (whose dequantized weights are 16 q).
+__device__ __forceinline__ uint4 sa_perm_x(uint4 v) {
+    uint32_t z = __byte_perm(v.x, v.z, 0x7632), w = __byte_perm(v.y, v.w, 0x7632);
+    const __half2 k = __float2half2_rn(0.0625f);
+    __half2 hz = __hmul2(*reinterpret_cast<__half2 *>(&z), k), hw = __hmul2(*reinterpret_cast<__half2 *>(&w), k);
+    return make_uint4(__byte_perm(v.x, v.z, 0x5410), __byte_perm(v.y, v.w, 0x5410),
+                      *reinterpret_cast<uint32_t *>(&hz), *reinterpret_cast<uint32_t *>(&hw));
+}
+
 template <int NT, bool XS>
 __device__ __forceinline__ void gemv_chunk_sa(int c, const uint32_t (&qa)[4], const uint32_t (&qb)[4], float sa,
                                               float sb, const uint32_t (&xaddr)[NT], const bool (&xon)[NT],
                                               const __half *const (&xg)[NT], uint4 (&xb)[NT],
                                               float (&acc)[2][NT][4]) {
-    float part[4][NT][4];
+    float part[2][NT][4];  // one chain per nibble class
 #pragma unroll
-    for (int a = 0; a < 4; ++a)
+    for (int a = 0; a < 2; ++a)
 #pragma unroll
         for (int j = 0; j < NT; ++j) part[a][j][0] = part[a][j][1] = part[a][j][2] = part[a][j][3] = 0.0f;
     const uint32_t k1032 = 0x64086408u;  // half2 (1032, 1032)
@@ -113,11 +127,7 @@ __device__ __forceinline__ void gemv_chunk_sa(int c, const uint32_t (&qa)[4], co
                     : "r"((int)xon[j]), "r"(addr));
             } else if (xon[j]) {
                 // natural order x0..x7 -> (x0,x4) (x2,x6) (x1,x5) (x3,x7)
-                const uint4 v = __ldg(reinterpret_cast<const uint4 *>(xg[j] + 128 * c + 8 * wd));
-                xb[j].x = __byte_perm(v.x, v.z, 0x5410);
-                xb[j].y = __byte_perm(v.y, v.w, 0x5410);
-                xb[j].z = __byte_perm(v.x, v.z, 0x7632);
-                xb[j].w = __byte_perm(v.y, v.w, 0x7632);
+                xb[j] = sa_perm_x(__ldg(reinterpret_cast<const uint4 *>(xg[j] + 128 * c + 8 * wd)));
             }
         }
         const uint32_t wa = qa[wd], wb = qb[wd];
@@ -130,7 +140,7 @@ __device__ __forceinline__ void gemv_chunk_sa(int c, const uint32_t (&qa)[4], co
             const uint32_t b2 = hsub2_u32(lop3_and_xor(wb8, 0x000F000Fu, 0x64086408u), k1032);
 #pragma unroll
             for (int j = 0; j < NT; ++j)
-                XTraits<__half>::mma(part[wd & 1][j], a0, b0, a2, b2, xb[j].x, xb[j].y);
+                XTraits<__half>::mma(part[0][j], a0, b0, a2, b2, xb[j].x, xb[j].y);
         }
         // class 1: (16 q1, 16 q5) and (16 q3, 16 q7)
         {
@@ -140,21 +150,16 @@ __device__ __forceinline__ void gemv_chunk_sa(int c, const uint32_t (&qa)[4], co
             const uint32_t b3 = hsub2_u32(lop3_and_xor(wb8, 0x00F000F0u, 0x64806480u), k1152);
 #pragma unroll
             for (int j = 0; j < NT; ++j)
-                XTraits<__half>::mma(part[2 + (wd & 1)][j], a1, b1, a3, b3, xb[j].z, xb[j].w);
+                XTraits<__half>::mma(part[1][j], a1, b1, a3, b3, xb[j].z, xb[j].w);
         }
     }
     // D fragment: elements 0, 1 belong to row g (scale sa), 2, 3 to row g+8.
-    const float sa16 = sa * 0.0625f, sb16 = sb * 0.0625f;
 #pragma unroll
     for (int j = 0; j < NT; ++j) {
         acc[0][j][0] = fmaf(part[0][j][0] + part[1][j][0], sa, acc[0][j][0]);
         acc[0][j][1] = fmaf(part[0][j][1] + part[1][j][1], sa, acc[0][j][1]);
         acc[0][j][2] = fmaf(part[0][j][2] + part[1][j][2], sb, acc[0][j][2]);
         acc[0][j][3] = fmaf(part[0][j][3] + part[1][j][3], sb, acc[0][j][3]);
-        acc[1][j][0] = fmaf(part[2][j][0] + part[3][j][0], sa16, acc[1][j][0]);
-        acc[1][j][1] = fmaf(part[2][j][1] + part[3][j][1], sa16, acc[1][j][1]);
-        acc[1][j][2] = fmaf(part[2][j][2] + part[3][j][2], sb16, acc[1][j][2]);
-        acc[1][j][3] = fmaf(part[2][j][3] + part[3][j][3], sb16, acc[1][j][3]);
     }
 }
 
@@ -237,8 +242,7 @@ __global__ void __launch_bounds__(WARPS * 32, MINB) gemv_int4_kernel(const XT *_
             const int r = i / rowv, c = i - r * rowv;
             uint4 v = c < kv ? __ldg(reinterpret_cast<const uint4 *>(x) + (size_t)r * kv + c) : make_uint4(0, 0, 0, 0);
             if (SA) {  // x0..x7 -> (x0,x4) (x2,x6) (x1,x5) (x3,x7)
-                v = make_uint4(__byte_perm(v.x, v.z, 0x5410), __byte_perm(v.y, v.w, 0x5410),
-                               __byte_perm(v.x, v.z, 0x7632), __byte_perm(v.y, v.w, 0x7632));
+                v = sa_perm_x(v);
             }
             xs_raw[i] = v;
         }
@@ -421,8 +425,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW <= 8 ? 2 : 1)
             const int r = i / rowv, c = i - r * rowv;
             uint4 v = c < kv ? __ldg(reinterpret_cast<const uint4 *>(x) + (size_t)r * kv + c) : make_uint4(0, 0, 0, 0);
             if (SA)
-                v = make_uint4(__byte_perm(v.x, v.z, 0x5410), __byte_perm(v.y, v.w, 0x5410),
-                               __byte_perm(v.x, v.z, 0x7632), __byte_perm(v.y, v.w, 0x7632));
+                v = sa_perm_x(v);
             reinterpret_cast<uint4 *>(xs)[i] = v;
         }
         asm volatile("bar.sync 1, %0;" ::"r"(CW * 32) : "memory");
@@ -591,8 +594,7 @@ __global__ void __launch_bounds__(256, 4)
             const int r = i / rowv, c = i - r * rowv;
             uint4 v = c < kv ? __ldg(reinterpret_cast<const uint4 *>(x) + (size_t)r * kv + c) : make_uint4(0, 0, 0, 0);
             if (SA)
-                v = make_uint4(__byte_perm(v.x, v.z, 0x5410), __byte_perm(v.y, v.w, 0x5410),
-                               __byte_perm(v.x, v.z, 0x7632), __byte_perm(v.y, v.w, 0x7632));
+                v = sa_perm_x(v);
             reinterpret_cast<uint4 *>(xs)[i] = v;
         }
     }
@@ -672,6 +674,160 @@ __global__ void __launch_bounds__(256, 4)
         float v = 0.0f;
 #pragma unroll
         for (int wv = 0; wv < CW; ++wv) v += red[wv][j][e][ln];
+        const int g2 = ln >> 2, t2 = ln & 3;
+        const int row = row0 + g2 + (e >= 2 ? 8 : 0);
+        const int mb = 8 * j + 2 * t2 + (e & 1);
+        if (ok && row < n && mb < m) y[(size_t)mb * n + row] = v;
+    }
+}
+
+// ----------------------------------------------------------- pair GEMV ----
+//
+// Small decode layers (KP <= 4096, at most two 16-row tiles per SM): one CTA
+// per SM, 16 warps, at most 64 registers, so exactly two CTAs fit on an SM.
+// In back-to-back launches every SM then holds one CTA of the previous launch
+// and receives exactly one of this one -- the placement stays balanced --
+// and this launch's weights (static) stream while the previous one finishes.
+// The CTA owns tiles blockIdx.x and blockIdx.x + gridDim.x; thread 0 issues
+// both tiles' TMA boxes at entry, and after griddepcontrol.wait warps 0-7
+// compute the first tile while warps 8-15 compute the second, each group with
+// gemv_tma_kernel's chunk -> warp map and fixed-order reduction (identical
+// results).
+template <typename XT, int NT, bool SA, bool XS, bool STMA>
+__global__ void __launch_bounds__(512, 2)
+    gemv_pair_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap smap,
+                     const XT *__restrict__ x, const float *__restrict__ scales, float *__restrict__ y, int m, int n,
+                     int k, int kp, int gshift, int xstride, int prefetch) {
+    static_assert(!SA || std::is_same<XT, __half>::value, "scale-after mode is for fp16 x");
+    constexpr int CW = 8, CPW = 4;
+    using L = TmaGemvLayout<CW, CPW>;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+    const int spr = L::kStageCols >> gshift;  // scales per row in a stage
+    const int sbytes = ((16 * spr * 4 + 127) / 128) * 128;
+    const int stage_bytes = L::kStageBytes + sbytes;                      // a multiple of 1024 + 128 k
+    const int stage_pitch = (stage_bytes + 1023) / 1024 * 1024;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + 2 * stage_pitch);
+    auto red = reinterpret_cast<float(*)[CW][NT][4][32]>(full + 2);      // [2 groups]
+    XT *xs = reinterpret_cast<XT *>(reinterpret_cast<uint8_t *>(red) + gemv_red_bytes(CW, NT));
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int grp = warp >> 3, wg = warp & 7;
+    const int gi = lane >> 2, t = lane & 3;
+    const int groups = kp >> gshift;
+    const int nchunks = (kp + 127) >> 7;
+    const int tiles = (n + 15) >> 4;
+    const int ntiles = (int)blockIdx.x + (int)gridDim.x < tiles ? 2 : 1;
+
+    asm volatile("griddepcontrol.launch_dependents;");
+    if (threadIdx.x == 0) {
+        mbar_init(&full[0], 1);
+        mbar_init(&full[1], 1);
+        fence_barrier_init();
+        tma_prefetch_desc(&wmap);
+        if (STMA) tma_prefetch_desc(&smap);
+        if (!prefetch) asm volatile("griddepcontrol.wait;" ::: "memory");
+        for (int tt = 0; tt < ntiles; ++tt) {
+            uint8_t *st = smem + tt * stage_pitch;
+            const int r0 = ((int)blockIdx.x + tt * (int)gridDim.x) * 16;
+            mbar_arrive_expect_tx(&full[tt], L::kStageBytes + (STMA ? 16 * spr * 4 : 0));
+#pragma unroll
+            for (int b = 0; b < L::kBoxes; ++b) tma_load_2d(st + b * 2048, &wmap, &full[tt], 128 * b, r0);
+            if (STMA) tma_load_2d(st + L::kStageBytes, &smap, &full[tt], 0, r0);
+        }
+    }
+
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (XS) {  // x [m][k] -> xs [m][xstride], zero beyond k (SA: pair-permuted)
+        const int rowv = xstride / 8, kv = k / 8;
+        for (int i = threadIdx.x; i < m * rowv; i += 512) {
+            const int r = i / rowv, c = i - r * rowv;
+            uint4 v = c < kv ? __ldg(reinterpret_cast<const uint4 *>(x) + (size_t)r * kv + c) : make_uint4(0, 0, 0, 0);
+            if (SA) v = sa_perm_x(v);
+            reinterpret_cast<uint4 *>(xs)[i] = v;
+        }
+    }
+    __syncthreads();  // xs staged; the barriers initialised before anyone waits on them
+    if (grp >= ntiles) return;  // no second tile: the second warp group is done
+
+    const uint8_t *wst = smem + grp * stage_pitch;
+    const float *sst = reinterpret_cast<const float *>(wst + L::kStageBytes);
+    const int row0 = ((int)blockIdx.x + grp * (int)gridDim.x) * 16;
+    uint32_t xaddr[NT];
+    bool xon[NT];
+    const XT *xg[NT];
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+        const int mb = 8 * j + gi;
+        xon[j] = mb < m;
+        const int mr = xon[j] ? mb : 0;
+        xaddr[j] = smem_u32(xs) + (uint32_t)(mr * xstride + 32 * t) * 2u;
+        xg[j] = x + (size_t)mr * k + 32 * t;
+    }
+    uint4 xb[NT];
+#pragma unroll
+    for (int j = 0; j < NT; ++j) xb[j] = make_uint4(0, 0, 0, 0);
+    float acc[2][NT][4];
+#pragma unroll
+    for (int a = 0; a < 2; ++a)
+#pragma unroll
+        for (int j = 0; j < NT; ++j) acc[a][j][0] = acc[a][j][1] = acc[a][j][2] = acc[a][j][3] = 0.0f;
+
+    float sreg[CPW][2];
+    if (!STMA) {  // scales straight from global memory (row pitch not 16-byte aligned)
+        const int ra = min(row0 + gi, n - 1), rb = min(row0 + gi + 8, n - 1);
+#pragma unroll
+        for (int q = 0; q < CPW; ++q) {
+            const int c = wg + q * CW;
+            const int col = min((128 * c + 32 * t) >> gshift, groups - 1);
+            sreg[q][0] = __ldg(scales + (size_t)ra * groups + col);
+            sreg[q][1] = __ldg(scales + (size_t)rb * groups + col);
+        }
+    }
+    const bool ok = mbar_wait(&full[grp], 0);
+    if (ok) {
+        auto do_chunk = [&](int q) {
+            const int c = wg + q * CW;
+            const uint32_t piece = (uint32_t)(c >> 1) * 2048u + (uint32_t)gi * 128u +
+                                   (uint32_t)(((((c & 1) << 2) + t) ^ (gi & 7)) << 4);
+            const uint4 wa = *reinterpret_cast<const uint4 *>(wst + piece);
+            const uint4 wb = *reinterpret_cast<const uint4 *>(wst + piece + 8 * 128);
+            const int scol = (c * 128 + 32 * t) >> gshift;
+            const float sa = STMA ? sst[gi * spr + scol] : sreg[q][0];
+            const float sb = STMA ? sst[(gi + 8) * spr + scol] : sreg[q][1];
+            const bool in = 128 * c + 32 * t < kp;
+            const uint32_t qa[4] = {wa.x, wa.y, wa.z, wa.w};
+            const uint32_t qb[4] = {wb.x, wb.y, wb.z, wb.w};
+            if constexpr (SA) {
+                gemv_chunk_sa<NT, XS>(c, qa, qb, in ? sa : 0.0f, in ? sb : 0.0f, xaddr, xon, xg, xb, acc);
+            } else {
+                const DqScale dsa = make_dq_scale(in ? sa : 0.0f), dsb = make_dq_scale(in ? sb : 0.0f);
+                if (__all_sync(0xffffffffu, dsa.fast && dsb.fast))
+                    gemv_chunk<XT, NT, XS, true>(c, qa, qb, dsa, dsb, xaddr, xon, xg, xb, acc);
+                else
+                    gemv_chunk<XT, NT, XS, false>(c, qa, qb, dsa, dsb, xaddr, xon, xg, xb, acc);
+            }
+        };
+        if ((CPW - 1) * CW + wg < nchunks) {
+#pragma unroll
+            for (int q = 0; q < CPW; ++q) do_chunk(q);
+        } else {
+#pragma unroll
+            for (int q = 0; q < CPW; ++q)
+                if (wg + q * CW < nchunks) do_chunk(q);
+        }
+    }
+    // Fixed-order reduction over the group's 8 warps (named barrier per group).
+#pragma unroll
+    for (int j = 0; j < NT; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) red[grp][wg][j][e][lane] = acc[0][j][e] + acc[1][j][e];
+    asm volatile("bar.sync %0, 256;" ::"r"(1 + grp) : "memory");
+    for (int idx = threadIdx.x & 255; idx < NT * 4 * 32; idx += 256) {
+        const int j = idx / 128, e = (idx / 32) % 4, ln = idx % 32;
+        float v = 0.0f;
+#pragma unroll
+        for (int wv = 0; wv < CW; ++wv) v += red[grp][wv][j][e][ln];
         const int g2 = ln >> 2, t2 = ln & 3;
         const int row = row0 + g2 + (e >= 2 ? 8 : 0);
         const int mb = 8 * j + 2 * t2 + (e & 1);
@@ -939,6 +1095,54 @@ int launch_gemv_tile(const XT *x, const uint8_t *packed, const float *scales, fl
     return stma ? pick(gemv_tile_kernel<XT, NT, SA, false, true>) : pick(gemv_tile_kernel<XT, NT, SA, false, false>);
 }
 
+// Pair GEMV (config 13): the tile GEMV's shapes with at most two tiles per SM.
+inline bool gemv_pair_ok(int64_t m, int64_t n, int64_t k, int64_t kp, int g, const uint8_t *packed) {
+    return gemv_tile_ok(m, n, k, kp, g, packed) && cdiv(n, 16) <= 2 * (int64_t)sm_count();
+}
+
+template <typename XT, int NT, bool SA>
+int launch_gemv_pair(const XT *x, const uint8_t *packed, const float *scales, float *y, int64_t m, int64_t n,
+                     int64_t k, int64_t kp, int g, int gshift, int prefetch, cudaStream_t st) {
+    using L = TmaGemvLayout<8, 4>;
+    if (!gemv_pair_ok(m, n, k, kp, g, packed)) return invalid("pair GEMV (config 13) does not take this shape");
+    const int64_t xstride = cdiv(kp, 128) * 128 + 8;
+    const size_t xbytes = (size_t)(m * xstride) * sizeof(XT);
+    const bool xs = (int64_t)xbytes <= kTileXs;
+    const size_t sbytes = (size_t)cdiv(16 * (L::kStageCols / g) * 4, 128) * 128;
+    const size_t pitch = (L::kStageBytes + sbytes + 1023) / 1024 * 1024;
+    const size_t smem = 1024 + 2 * pitch + 16 + gemv_red_bytes(8, NT) + (xs ? xbytes : 0);
+    const int64_t tiles = cdiv(n, 16);
+    const int64_t grid = std::min<int64_t>(tiles, sm_count());
+    CUtensorMap wmap, smap;
+    bool stma = false;
+    int rc = make_gemv_maps<8, 4>(packed, scales, n, kp, g, &wmap, &smap, &stma);
+    if (rc != OQ_OK) return rc;
+    auto pick = [&](auto kern) -> int {
+        int rc2 = allow_dynamic_smem(reinterpret_cast<const void *>(kern), smem);
+        if (rc2 != OQ_OK) return rc2;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)grid);
+        cfg.blockDim = dim3(512);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        cudaError_t err = cudaLaunchKernelEx(&cfg, kern, wmap, smap, x, scales, y, (int)m, (int)n, (int)k, (int)kp,
+                                             gshift, (int)xstride, prefetch);
+        if (err != cudaSuccess) {
+            set_error("int4_linear (pair GEMV): launch failed: %s", cudaGetErrorString(err));
+            return OQ_ERR_CUDA;
+        }
+        return OQ_OK;
+    };
+    if (xs)
+        return stma ? pick(gemv_pair_kernel<XT, NT, SA, true, true>) : pick(gemv_pair_kernel<XT, NT, SA, true, false>);
+    return stma ? pick(gemv_pair_kernel<XT, NT, SA, false, true>) : pick(gemv_pair_kernel<XT, NT, SA, false, false>);
+}
+
 // True when the TMA GEMV takes this shape (M <= 16, 32 <= g <= the stage
 // width, packed rows 16-byte aligned, and the shared-memory plan fits).
 template <int CW, int CPW, int CTAS = 1>
@@ -962,11 +1166,14 @@ bool tma_gemv_ok(int64_t m, int64_t k, int64_t kp, int g, const uint8_t *packed)
 //   12    one CTA of 8 warps per 16-row tile, no producer warp, four CTAs
 //         per SM (KP <= 4096, M <= 16): the next launch's CTAs fit beside
 //         this one's, so back-to-back GEMVs overlap (PDL)
+//   13    one CTA of 16 warps per SM owning two tiles (KP <= 4096, at most
+//         two tiles per SM, M <= 16): balanced placement in back-to-back
+//         launches, the next launch's weights stream meanwhile
 // config & 16 (OQ_CONFIG_EXACT_ROUNDING) forces the exact weight rounding
 // for fp16 x, which otherwise uses the scale-after path when g % 128 == 0.
 // config & 32 (OQ_CONFIG_STATIC_WEIGHTS) lets the weights and scales stream
 // before the wait on the previous kernel in the stream.
-constexpr int kGemvConfigs = 12;
+constexpr int kGemvConfigs = 13;
 
 template <typename XT, int NT, bool SA>
 int launch_gemv_nt(int config, const XT *x, const uint8_t *packed, const float *scales, float *y, int64_t m,
@@ -991,6 +1198,9 @@ int launch_gemv_nt(int config, const XT *x, const uint8_t *packed, const float *
         case 12:
             if constexpr (NT <= 2) return launch_gemv_tile<XT, NT, SA>(x, packed, scales, y, m, n, k, kp, g, gshift, pf, st);
             return invalid("tile GEMV needs M <= 16");
+        case 13:
+            if constexpr (NT <= 2) return launch_gemv_pair<XT, NT, SA>(x, packed, scales, y, m, n, k, kp, g, gshift, pf, st);
+            return invalid("pair GEMV needs M <= 16");
         default: return launch_gemv_t<XT, NT, 8, 2, 3, SA>(x, packed, scales, y, m, n, k, kp, gshift, pf, st);
     }
 }
@@ -1015,7 +1225,9 @@ int launch_gemv(const XT *x, const uint8_t *packed, const float *scales, float *
     int shape = config & 15;
     const bool auto_shape = shape <= 0 || shape > kGemvConfigs;
     if (auto_shape) {
-        if (nt == 1 && tma_gemv_ok<8, 4, 2>(m, k, kp, g, packed))
+        if (gemv_pair_ok(m, n, k, kp, g, packed))
+            shape = 13;
+        else if (nt == 1 && tma_gemv_ok<8, 4, 2>(m, k, kp, g, packed))
             shape = 10;
         else if (tma_gemv_ok<16, 2>(m, k, kp, g, packed))
             shape = 9;

@@ -74,12 +74,13 @@ def test_reference_test_shapes(shape, dtype):
     check_against_oracle(y, x, q, g, dtype)
 
 
-@pytest.mark.parametrize("cfg", [8, 9, 10, 12, 8 | 16, 9 | 16, 12 | 16, 10 | 32, 12 | 32])
+@pytest.mark.parametrize("cfg", [8, 9, 10, 12, 13, 8 | 16, 9 | 16, 12 | 16, 13 | 16, 10 | 32, 12 | 32, 13 | 32])
 @pytest.mark.parametrize("shape", [(1, 4096, 4096, 128), (1, 1000, 11008, 128), (16, 300, 4096, 64),
                                    (9, 77, 1000, 32), (2, 4097, 1152, 256), (1, 16, 8, 32), (5, 40, 3000, 128)])
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
 def test_tma_gemv_vs_oracle(shape, dtype, cfg):
-    """The TMA-fed GEMVs (configs 8-10 persistent, 12 one CTA per tile;
+    """The TMA-fed GEMVs (configs 8-10 persistent, 12 one CTA per tile, 13
+    one CTA per SM owning two tiles;
     | 16 = exact rounding, | 32 = static weights streamed before the wait on
     the previous kernel)."""
     from openquant_b200 import _native as nat
@@ -114,7 +115,7 @@ def test_static_weights_same_result_and_ordering(shape):
     x, q, xt = make_case(m, n, k, g, torch.float16, seed=n + k, w_sigma=0.02)
     p, s = torch.from_numpy(q.data).cuda(), torch.from_numpy(q.scales).cuda()
     lib = nat.load()
-    for cfg in (0, 1, 8, 10, 12):
+    for cfg in (0, 1, 8, 10, 12, 13):
         outs = []
         for flag in (0, nat.CONFIG_STATIC_WEIGHTS):
             y = torch.full((m, n), float("nan"), device="cuda")
