@@ -102,12 +102,60 @@ __device__ __forceinline__ uint4 sa_perm_x(uint4 v) {
                       *reinterpret_cast<uint32_t *>(&hz), *reinterpret_cast<uint32_t *>(&hw));
 }
 
-template <int NT, bool XS>
+// x [m][k] -> xs [m][xstride] (zero beyond k; SA: the scale-after layout).
+// FOLD also fills corr[c][r] (r < m, 128-column chunk c) = 1032 * (sum of the
+// chunk's class-0 x of row r) + 1152 * (sum of its class-1 x / 16), in a fixed
+// order: with KP % 128 == 0, thread i stages vector i % (KP/8) of row
+// i / (KP/8), so a chunk's 16 vectors lie in 16 aligned lanes and a
+// shuffle tree sums them.  All threads of the block call it.
+template <typename XT, bool SA, bool FOLD>
+__device__ __forceinline__ void gemv_stage_x(const XT *__restrict__ x, XT *xs, float *corr, int m, int k, int kp,
+                                             int xstride, int nthreads) {
+    if (!FOLD) {
+        const int rowv = xstride / 8, kv = k / 8;
+        for (int i = threadIdx.x; i < m * rowv; i += nthreads) {
+            const int r = i / rowv, c = i - r * rowv;
+            uint4 v = c < kv ? __ldg(reinterpret_cast<const uint4 *>(x) + (size_t)r * kv + c) : make_uint4(0, 0, 0, 0);
+            if (SA) v = sa_perm_x(v);
+            reinterpret_cast<uint4 *>(xs)[i] = v;
+        }
+    } else {
+        const int kv8 = kp / 8, kv = k / 8, total = m * kv8;
+        for (int i0 = (int)threadIdx.x - (int)(threadIdx.x & 31); i0 < total; i0 += nthreads) {
+            const int i = i0 + (int)(threadIdx.x & 31);
+            const bool live = i < total;
+            const int r = live ? i / kv8 : 0, cv = live ? i - r * kv8 : 0;
+            uint4 v = make_uint4(0, 0, 0, 0);
+            if (live && cv < kv) v = __ldg(reinterpret_cast<const uint4 *>(x) + (size_t)r * kv + cv);
+            v = sa_perm_x(v);
+            if (live) reinterpret_cast<uint4 *>(xs)[r * (xstride / 8) + cv] = v;
+            const float2 f0 = __half22float2(*reinterpret_cast<const __half2 *>(&v.x));
+            const float2 f1 = __half22float2(*reinterpret_cast<const __half2 *>(&v.y));
+            const float2 f2 = __half22float2(*reinterpret_cast<const __half2 *>(&v.z));
+            const float2 f3 = __half22float2(*reinterpret_cast<const __half2 *>(&v.w));
+            float t = 1032.0f * ((f0.x + f0.y) + (f1.x + f1.y)) + 1152.0f * ((f2.x + f2.y) + (f3.x + f3.y));
+#pragma unroll
+            for (int o = 8; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+            if (live && (cv & 15) == 0) corr[(cv >> 4) * 16 + r] = t;
+        }
+    }
+}
+
+// FOLD (staged x only): the biased halves (1032 + q, 1152 + 16 q) go to the
+// tensor core as they are -- no HSUB2 -- and the bias's share of each sum,
+// 1032 * (sum of the chunk's class-0 x) + 1152 * (sum of its class-1 x / 16)
+// for batch row n, is subtracted once per chunk: corr_ct points at
+// corr[c][2t] of a [chunk][16 batch rows] table (gemv_fold_corr).  Products
+// stay exact; the fp32 sums grow to ~1e3 |x|, so the result carries ~1e-3
+// absolute error per chunk (~1e-5 relative in y), below the reference's own
+// fp16 weight rounding.
+template <int NT, bool XS, bool FOLD = false>
 __device__ __forceinline__ void gemv_chunk_sa(int c, const uint32_t (&qa)[4], const uint32_t (&qb)[4], float sa,
                                               float sb, const uint32_t (&xaddr)[NT], const bool (&xon)[NT],
                                               const __half *const (&xg)[NT], uint4 (&xb)[NT],
-                                              float (&acc)[2][NT][4]) {
-    float part[2][NT][4];  // one chain per nibble class
+                                              float (&acc)[2][NT][4], const float *corr_ct = nullptr) {
+    static_assert(!FOLD || XS, "the bias correction needs staged x");
+    float part[2][NT][4];  // one accumulator chain per nibble class
 #pragma unroll
     for (int a = 0; a < 2; ++a)
 #pragma unroll
@@ -134,32 +182,42 @@ __device__ __forceinline__ void gemv_chunk_sa(int c, const uint32_t (&qa)[4], co
         const uint32_t wa8 = wa >> 8, wb8 = wb >> 8;
         // class 0: (q0, q4) and (q2, q6)
         {
-            const uint32_t a0 = hsub2_u32(lop3_and_xor(wa, 0x000F000Fu, 0x64086408u), k1032);
-            const uint32_t a2 = hsub2_u32(lop3_and_xor(wa8, 0x000F000Fu, 0x64086408u), k1032);
-            const uint32_t b0 = hsub2_u32(lop3_and_xor(wb, 0x000F000Fu, 0x64086408u), k1032);
-            const uint32_t b2 = hsub2_u32(lop3_and_xor(wb8, 0x000F000Fu, 0x64086408u), k1032);
+            uint32_t a0 = lop3_and_xor(wa, 0x000F000Fu, 0x64086408u), a2 = lop3_and_xor(wa8, 0x000F000Fu, 0x64086408u);
+            uint32_t b0 = lop3_and_xor(wb, 0x000F000Fu, 0x64086408u), b2 = lop3_and_xor(wb8, 0x000F000Fu, 0x64086408u);
+            if (!FOLD) {
+                a0 = hsub2_u32(a0, k1032), a2 = hsub2_u32(a2, k1032);
+                b0 = hsub2_u32(b0, k1032), b2 = hsub2_u32(b2, k1032);
+            }
 #pragma unroll
             for (int j = 0; j < NT; ++j)
                 XTraits<__half>::mma(part[0][j], a0, b0, a2, b2, xb[j].x, xb[j].y);
         }
         // class 1: (16 q1, 16 q5) and (16 q3, 16 q7)
         {
-            const uint32_t a1 = hsub2_u32(lop3_and_xor(wa, 0x00F000F0u, 0x64806480u), k1152);
-            const uint32_t a3 = hsub2_u32(lop3_and_xor(wa8, 0x00F000F0u, 0x64806480u), k1152);
-            const uint32_t b1 = hsub2_u32(lop3_and_xor(wb, 0x00F000F0u, 0x64806480u), k1152);
-            const uint32_t b3 = hsub2_u32(lop3_and_xor(wb8, 0x00F000F0u, 0x64806480u), k1152);
+            uint32_t a1 = lop3_and_xor(wa, 0x00F000F0u, 0x64806480u), a3 = lop3_and_xor(wa8, 0x00F000F0u, 0x64806480u);
+            uint32_t b1 = lop3_and_xor(wb, 0x00F000F0u, 0x64806480u), b3 = lop3_and_xor(wb8, 0x00F000F0u, 0x64806480u);
+            if (!FOLD) {
+                a1 = hsub2_u32(a1, k1152), a3 = hsub2_u32(a3, k1152);
+                b1 = hsub2_u32(b1, k1152), b3 = hsub2_u32(b3, k1152);
+            }
 #pragma unroll
             for (int j = 0; j < NT; ++j)
                 XTraits<__half>::mma(part[1][j], a1, b1, a3, b3, xb[j].z, xb[j].w);
         }
     }
-    // D fragment: elements 0, 1 belong to row g (scale sa), 2, 3 to row g+8.
+    // D fragment: elements 0, 1 belong to row g (scale sa), 2, 3 to row g+8;
+    // elements 0, 2 to batch row 8j + 2t, 1, 3 to 8j + 2t + 1.
 #pragma unroll
     for (int j = 0; j < NT; ++j) {
-        acc[0][j][0] = fmaf(part[0][j][0] + part[1][j][0], sa, acc[0][j][0]);
-        acc[0][j][1] = fmaf(part[0][j][1] + part[1][j][1], sa, acc[0][j][1]);
-        acc[0][j][2] = fmaf(part[0][j][2] + part[1][j][2], sb, acc[0][j][2]);
-        acc[0][j][3] = fmaf(part[0][j][3] + part[1][j][3], sb, acc[0][j][3]);
+        float c0 = 0.0f, c1 = 0.0f;
+        if (FOLD) {
+            const float2 cv = *reinterpret_cast<const float2 *>(corr_ct + 8 * j);
+            c0 = cv.x, c1 = cv.y;
+        }
+        acc[0][j][0] = fmaf(part[0][j][0] + part[1][j][0] - c0, sa, acc[0][j][0]);
+        acc[0][j][1] = fmaf(part[0][j][1] + part[1][j][1] - c1, sa, acc[0][j][1]);
+        acc[0][j][2] = fmaf(part[0][j][2] + part[1][j][2] - c0, sb, acc[0][j][2]);
+        acc[0][j][3] = fmaf(part[0][j][3] + part[1][j][3] - c1, sb, acc[0][j][3]);
     }
 }
 
@@ -564,6 +622,8 @@ __global__ void __launch_bounds__(256, 4)
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + L::kStageBytes + sbytes);
     auto red = reinterpret_cast<float(*)[NT][4][32]>(full + 2);              // [CW]
     XT *xs = reinterpret_cast<XT *>(reinterpret_cast<uint8_t *>(red) + gemv_red_bytes(CW, NT) / 2);
+    constexpr bool FOLD = SA && XS;  // bias-folded dequantization (gemv_chunk_sa)
+    float *corr = reinterpret_cast<float *>(xs + (size_t)m * xstride);  // [chunks][16]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int gi = lane >> 2, t = lane & 3;
@@ -588,16 +648,7 @@ __global__ void __launch_bounds__(256, 4)
     }
 
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    if (XS) {  // x [m][k] -> xs [m][xstride], zero beyond k (SA: pair-permuted)
-        const int rowv = xstride / 8, kv = k / 8;
-        for (int i = threadIdx.x; i < m * rowv; i += CW * 32) {
-            const int r = i / rowv, c = i - r * rowv;
-            uint4 v = c < kv ? __ldg(reinterpret_cast<const uint4 *>(x) + (size_t)r * kv + c) : make_uint4(0, 0, 0, 0);
-            if (SA)
-                v = sa_perm_x(v);
-            reinterpret_cast<uint4 *>(xs)[i] = v;
-        }
-    }
+    if (XS) gemv_stage_x<XT, SA, FOLD>(x, xs, corr, m, k, kp, xstride, CW * 32);
     __syncthreads();  // xs staged; full[0] initialised before anyone waits on it
     uint32_t xaddr[NT];
     bool xon[NT];
@@ -645,7 +696,8 @@ __global__ void __launch_bounds__(256, 4)
             const uint32_t qa[4] = {wa.x, wa.y, wa.z, wa.w};
             const uint32_t qb[4] = {wb.x, wb.y, wb.z, wb.w};
             if constexpr (SA) {
-                gemv_chunk_sa<NT, XS>(c, qa, qb, in ? sa : 0.0f, in ? sb : 0.0f, xaddr, xon, xg, xb, acc);
+                gemv_chunk_sa<NT, XS, FOLD>(c, qa, qb, in ? sa : 0.0f, in ? sb : 0.0f, xaddr, xon, xg, xb, acc,
+                                            corr + c * 16 + 2 * t);
             } else {
                 const DqScale dsa = make_dq_scale(in ? sa : 0.0f), dsb = make_dq_scale(in ? sb : 0.0f);
                 if (__all_sync(0xffffffffu, dsa.fast && dsb.fast))
@@ -710,6 +762,8 @@ __global__ void __launch_bounds__(512, 2)
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + 2 * stage_pitch);
     auto red = reinterpret_cast<float(*)[CW][NT][4][32]>(full + 2);      // [2 groups]
     XT *xs = reinterpret_cast<XT *>(reinterpret_cast<uint8_t *>(red) + gemv_red_bytes(CW, NT));
+    constexpr bool FOLD = SA && XS;  // bias-folded dequantization (gemv_chunk_sa)
+    float *corr = reinterpret_cast<float *>(xs + (size_t)m * xstride);  // [chunks][16]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int grp = warp >> 3, wg = warp & 7;
@@ -738,15 +792,7 @@ __global__ void __launch_bounds__(512, 2)
     }
 
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    if (XS) {  // x [m][k] -> xs [m][xstride], zero beyond k (SA: pair-permuted)
-        const int rowv = xstride / 8, kv = k / 8;
-        for (int i = threadIdx.x; i < m * rowv; i += 512) {
-            const int r = i / rowv, c = i - r * rowv;
-            uint4 v = c < kv ? __ldg(reinterpret_cast<const uint4 *>(x) + (size_t)r * kv + c) : make_uint4(0, 0, 0, 0);
-            if (SA) v = sa_perm_x(v);
-            reinterpret_cast<uint4 *>(xs)[i] = v;
-        }
-    }
+    if (XS) gemv_stage_x<XT, SA, FOLD>(x, xs, corr, m, k, kp, xstride, 512);
     __syncthreads();  // xs staged; the barriers initialised before anyone waits on them
     if (grp >= ntiles) return;  // no second tile: the second warp group is done
 
@@ -799,7 +845,8 @@ __global__ void __launch_bounds__(512, 2)
             const uint32_t qa[4] = {wa.x, wa.y, wa.z, wa.w};
             const uint32_t qb[4] = {wb.x, wb.y, wb.z, wb.w};
             if constexpr (SA) {
-                gemv_chunk_sa<NT, XS>(c, qa, qb, in ? sa : 0.0f, in ? sb : 0.0f, xaddr, xon, xg, xb, acc);
+                gemv_chunk_sa<NT, XS, FOLD>(c, qa, qb, in ? sa : 0.0f, in ? sb : 0.0f, xaddr, xon, xg, xb, acc,
+                                            corr + c * 16 + 2 * t);
             } else {
                 const DqScale dsa = make_dq_scale(in ? sa : 0.0f), dsb = make_dq_scale(in ? sb : 0.0f);
                 if (__all_sync(0xffffffffu, dsa.fast && dsb.fast))
@@ -1064,7 +1111,8 @@ int launch_gemv_tile(const XT *x, const uint8_t *packed, const float *scales, fl
     const size_t xbytes = (size_t)(m * xstride) * sizeof(XT);
     const bool xs = (int64_t)xbytes <= kTileXs;
     const size_t sbytes = (size_t)cdiv(16 * (L::kStageCols / g) * 4, 128) * 128;
-    const size_t smem = 1024 + L::kStageBytes + sbytes + 16 + gemv_red_bytes(8, NT) / 2 + (xs ? xbytes : 0);
+    const size_t cbytes = (SA && xs) ? (size_t)cdiv(kp, 128) * 16 * 4 : 0;  // bias table
+    const size_t smem = 1024 + L::kStageBytes + sbytes + 16 + gemv_red_bytes(8, NT) / 2 + (xs ? xbytes : 0) + cbytes;
     CUtensorMap wmap, smap;
     bool stma = false;
     int rc = make_gemv_maps<8, 4>(packed, scales, n, kp, g, &wmap, &smap, &stma);
@@ -1110,7 +1158,8 @@ int launch_gemv_pair(const XT *x, const uint8_t *packed, const float *scales, fl
     const bool xs = (int64_t)xbytes <= kTileXs;
     const size_t sbytes = (size_t)cdiv(16 * (L::kStageCols / g) * 4, 128) * 128;
     const size_t pitch = (L::kStageBytes + sbytes + 1023) / 1024 * 1024;
-    const size_t smem = 1024 + 2 * pitch + 16 + gemv_red_bytes(8, NT) + (xs ? xbytes : 0);
+    const size_t cbytes = (SA && xs) ? (size_t)cdiv(kp, 128) * 16 * 4 : 0;  // bias table
+    const size_t smem = 1024 + 2 * pitch + 16 + gemv_red_bytes(8, NT) + (xs ? xbytes : 0) + cbytes;
     const int64_t tiles = cdiv(n, 16);
     const int64_t grid = std::min<int64_t>(tiles, sm_count());
     CUtensorMap wmap, smap;
