@@ -328,6 +328,75 @@ def measure_gemm(dev, peaks, steps=10, warmup=3):
     }
 
 
+def measure_w8a8(dev, peaks, steps=10, warmup=3):
+    """TOPS of the W8A8 GEMM (per-token INT8 x, per-row INT8 W, tcgen05
+    kind::i8) at M = 2048, (K, N) = (8192, 28672), two weight copies
+    alternated (2 x 235 MB, beyond L2); CUDA-graph replay, CUDA events.  The
+    roofline peak is twice the measured bf16 GEMM rate (the B200's dense INT8
+    rate is twice its BF16 rate; no INT8 peak is measured)."""
+    import ctypes
+
+    import torch
+
+    from openquant_b200 import _native as nat
+
+    lib = nat.load()
+    m, k, n = 2048, 8192, 28672
+    gen = torch.Generator(device=dev).manual_seed(81)
+    qws = [torch.randint(-127, 128, (n, k), generator=gen, device=dev, dtype=torch.int8) for _ in range(2)]
+    sw = torch.rand(n, generator=gen, device=dev) * 0.01 + 1e-3
+    qx = torch.randint(-127, 128, (m, k), generator=gen, device=dev, dtype=torch.int8)
+    sx = torch.rand(m, generator=gen, device=dev) * 0.01 + 1e-3
+    y = torch.empty(m, n, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+
+    def launch(count, h):
+        for i in range(count):
+            st = lib.oq_int8_gemm(ctypes.c_void_p(qx.data_ptr()), ctypes.c_void_p(sx.data_ptr()),
+                                  ctypes.c_void_p(qws[i % 2].data_ptr()), ctypes.c_void_p(sw.data_ptr()),
+                                  ctypes.c_void_p(y.data_ptr()), m, n, k, h)
+            if st != 0:
+                raise RuntimeError(nat.last_error())
+
+    with torch.cuda.stream(stream):
+        launch(warmup, ctypes.c_void_p(stream.cuda_stream))
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        launch(steps, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    graph.replay()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        graph.replay()
+        end.record(stream)
+    torch.cuda.synchronize()
+    del graph
+    ms = start.elapsed_time(end) / steps
+    tops = 2.0 * m * n * k / (ms / 1e3) / 1e12
+    # exact check on sampled columns: the int32 sums are exact, the epilogue rounds three times
+    cols = torch.arange(0, n, 1021, device=dev)
+    w = qws[(steps - 1) % 2]
+    ref = (qx.double() @ w[cols].double().T) * sx.double()[:, None] * sw[cols].double()[None, :]
+    rel = float(((y[:, cols].double() - ref).abs() / ref.abs().clamp_min(1e-30)).max())
+    assert rel < 4e-7, rel
+    peak = 2.0 * peaks["bf16_tflops"]
+    return {
+        "metric": "W8A8 GEMM TOPS at M=2048 (per-token INT8 x, per-row INT8 W)",
+        "workload": "int8_gemm_m2048_k8192_n28672",
+        "value": tops,
+        "unit": "TOPS",
+        "ms_per_step": ms,
+        "steps": steps,
+        "roofline": {"bound": "tensor", "achieved": tops, "peak": peak, "unit": "TOPS", "frac": tops / peak,
+                     "peak_source": "2 x measured bf16 GEMM TFLOP/s (dense INT8 rate is twice BF16)",
+                     "algorithmic_ops_per_launch": 2 * m * n * k},
+        "gpu_launches": steps,
+        "check_max_rel_err": rel,
+    }
+
+
 # One Llama-3-70B decoder layer: (rows = out features, cols = in features)
 # of its seven projection matrices; 855,638,016 weights.
 BULK_SHAPES = [("q_proj", 8192, 8192), ("k_proj", 1024, 8192), ("v_proj", 1024, 8192), ("o_proj", 8192, 8192),
@@ -750,7 +819,7 @@ def run_ours(args):
     if not args.no_gemm:
         sys.path.insert(0, os.path.join(ROOT, "oracle"))
         if world == 1:
-            line["also"] = [measure_gemm(dev, peaks)]
+            line["also"] = [measure_gemm(dev, peaks), measure_w8a8(dev, peaks)]
         else:
             line["also"] = [measure_sharded_gemm(dev, world, rank, peaks)]
     if not args.no_bulk:

@@ -196,6 +196,21 @@ OQ_API int oq_int4_linear(const void *x, int x_dtype, const uint8_t *packed,
                    int64_t k, int group_size, int kernel, int config,
                    oq_stream_t stream);
 
+/* W8A8 linear layer on the tcgen05 tensor cores (kind::i8, int32 sums):
+ * y[m][n] = sx[m] * sw[n] * sum_k qx[m][k] * qw[n][k].  qx / sx and qw / sw
+ * are per-row INT8 data and fp32 scales in the format of
+ * oq_quant_int8_rowwise (the reference's quantize(bits=8),
+ * openquant/quantization.py:14-40) -- for the activations, one row per token.
+ *   qx : int8 [M][K], sx : fp32 [M]   (device)
+ *   qw : int8 [N][K], sw : fp32 [N]   (device)
+ *   y  : fp32 [M][N]                  (device, out)
+ * K % 16 == 0, qx and qw 16-byte aligned.  No counterpart in the reference
+ * (its only matmul is the INT4 one); this is the activation-side extension of
+ * the same per-row INT8 format. */
+OQ_API int oq_int8_gemm(const int8_t *qx, const float *sx, const int8_t *qw,
+                        const float *sw, float *y, int64_t m, int64_t n,
+                        int64_t k, oq_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

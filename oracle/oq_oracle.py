@@ -175,3 +175,17 @@ def threaded_rows(fn, rows, threads=None, min_rows=64):
         return [fn(0, rows)]
     with ThreadPoolExecutor(max_workers=blocks) as pool:
         return list(pool.map(lambda i: fn(edges[i], edges[i + 1]), range(blocks)))
+
+
+def int8_matmul(qx, sx, qw, sw):
+    """y[m, n] = sx[m] * sw[n] * sum_k qx[m, k] qw[n, k] in float64.
+
+    The W8A8 product of two per-row INT8 operands in the format of quantize
+    (quantization.py:23-37).  The integer sums are exact in float64 while
+    K * 127^2 < 2^53.
+    """
+    qx = np.asarray(qx, dtype=np.float64)
+    qw = np.asarray(qw, dtype=np.float64)
+    sx = np.asarray(sx, dtype=np.float64).reshape(-1, 1)
+    sw = np.asarray(sw, dtype=np.float64).reshape(1, -1)
+    return (qx @ qw.T) * sx * sw
