@@ -72,3 +72,22 @@ def test_cli_tune_quick(tmp_path):
     data = json.loads(out.read_text())
     assert len(data["entries"]) == 1 and data["entries"][0]["key"] == [128, 2048, 2048, 32]
     tile_table.reset()
+
+
+def test_gpu_report_schema_2(tmp_path):
+    from openquant.cli import main
+
+    out = tmp_path / "gpu.json"
+    assert main(["report", "--gpu", "--rows", "512", "--cols", "1024", "--group-size", "128", "--batch", "4",
+                 "--output", str(out)]) == 0
+    data = json.loads(out.read_text(encoding="utf-8"))
+    assert data["schema_version"] == 2 and data["weights"]["shape"] == [512, 1024]
+    fm = data["gpu"]["formats"]
+    assert set(fm) == {"INT8", "INT4", "INT4_GROUP_128"}
+    assert {"quantize_fp16", "dequantize", "w8a8_linear"} <= set(fm["INT8"])
+    assert "int4_linear" in fm["INT4_GROUP_128"]
+    for kernels in fm.values():
+        for k in kernels.values():
+            assert k["time_us"] > 0 and k["GB_per_s"] > 0
+    # schema-1 content is unchanged
+    assert data["formats"]["INT4_GROUP_128"]["storage_bytes"] == 512 * 1024 // 2 + 512 * 8 * 4
