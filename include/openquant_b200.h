@@ -196,6 +196,18 @@ OQ_API int oq_int4_linear(const void *x, int x_dtype, const uint8_t *packed,
                    int64_t k, int group_size, int kernel, int config,
                    oq_stream_t stream);
 
+/* oq_int4_linear with a fused epilogue: y[m][n] = (x . W^T)[m][n] + bias[n],
+ * written as fp32, fp16 or bf16 (y_dtype = OQ_F32 / OQ_F16 / OQ_BF16) --
+ * the bias is added in fp32 and the sum rounded once to y_dtype.  bias may be
+ * NULL (fp32 [N] otherwise, device).  Every other argument as oq_int4_linear.
+ * No counterpart in the reference (its kernel writes fp32 only,
+ * openquant/triton_int4.py:120-122). */
+OQ_API int oq_int4_linear_ex(const void *x, int x_dtype, const uint8_t *packed,
+                             const float *scales, void *y, int y_dtype,
+                             const float *bias, int64_t m, int64_t n, int64_t k,
+                             int group_size, int kernel, int config,
+                             oq_stream_t stream);
+
 /* W8A8 linear layer on the tcgen05 tensor cores (kind::i8, int32 sums):
  * y[m][n] = sx[m] * sw[n] * sum_k qx[m][k] * qw[n][k].  qx / sx and qw / sw
  * are per-row INT8 data and fp32 scales in the format of

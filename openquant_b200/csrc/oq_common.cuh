@@ -54,6 +54,24 @@ inline int dtype_size(int dtype) {
 }
 
 // Number of SMs of the current device (cached per device).
+// Output of a linear layer: y[b][feature] as fp32, fp16 or bf16 (OQ_F32 /
+// OQ_F16 / OQ_BF16), with an optional fp32 bias per output feature added in
+// fp32 before the single rounding to the output type.
+struct OutSpec {
+    void *y;
+    const float *bias;  // nullptr: no bias
+    int dtype;
+    __device__ __forceinline__ void store(size_t idx, int feature, float v) const {
+        if (bias != nullptr) v += __ldg(bias + feature);
+        if (dtype == OQ_F16)
+            static_cast<__half *>(y)[idx] = __float2half_rn(v);
+        else if (dtype == OQ_BF16)
+            static_cast<__nv_bfloat16 *>(y)[idx] = __float2bfloat16_rn(v);
+        else
+            static_cast<float *>(y)[idx] = v;
+    }
+};
+
 int sm_count();
 // Raises a kernel's dynamic shared-memory limit to `bytes` on the current
 // device (once per kernel, device and size; thread-safe).

@@ -58,7 +58,7 @@ static_assert(kAccCols + kStages * kACols <= kTmemCols, "TMEM budget");
 template <typename XT>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_int4_tcgen05_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
-                             const float *__restrict__ scales, float *__restrict__ y, int m, int n, int kp, int g) {
+                             const float *__restrict__ scales, OutSpec y, int m, int n, int kp, int g) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
     uint8_t *xbuf = smem;                                    // [S][256 rows][128 B], swizzled
@@ -216,7 +216,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int j = 0; j < 32; ++j) {
                         const int mb = m0 + c * 32 + j;
-                        if (mb < m) y[(size_t)mb * n + row] = __uint_as_float(v[j]);
+                        if (mb < m) y.store((size_t)mb * n + row, row, __uint_as_float(v[j]));
                     }
                 }
             }
@@ -246,7 +246,7 @@ int allow_smem(const void *kern, size_t bytes) {
 }
 
 template <typename XT>
-int launch(const XT *x, CUtensorMapDataType xtype, const uint8_t *packed, const float *scales, float *y, int64_t m,
+int launch(const XT *x, CUtensorMapDataType xtype, const uint8_t *packed, const float *scales, OutSpec y, int64_t m,
            int64_t n, int64_t k, int g, cudaStream_t st) {
     const int64_t kp = cdiv(k, g) * g;
     CUtensorMap xmap, wmap;
@@ -294,7 +294,7 @@ int gemm_tcgen05_supported(int64_t m, int64_t n, int64_t k, int g, const void *x
     return 1;
 }
 
-int gemm_tcgen05_launch(const void *x, int x_dtype, const uint8_t *packed, const float *scales, float *y, int64_t m,
+int gemm_tcgen05_launch(const void *x, int x_dtype, const uint8_t *packed, const float *scales, OutSpec y, int64_t m,
                         int64_t n, int64_t k, int g, cudaStream_t st) {
     if (x_dtype == OQ_BF16)
         return launch(static_cast<const __nv_bfloat16 *>(x), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, packed, scales, y, m,

@@ -16,7 +16,7 @@ namespace oq {
 
 int gemm_tcgen05_supported(int64_t m, int64_t n, int64_t k, int g, const void *x, const uint8_t *packed,
                            const float *y);
-int gemm_tcgen05_launch(const void *x, int x_dtype, const uint8_t *packed, const float *scales, float *y,
+int gemm_tcgen05_launch(const void *x, int x_dtype, const uint8_t *packed, const float *scales, OutSpec y,
                         int64_t m, int64_t n, int64_t k, int g, cudaStream_t st);
 
 namespace {
@@ -225,7 +225,7 @@ template <typename XT, int NT, int WARPS, int U, bool XS, int MINB, bool SA>
 __global__ void __launch_bounds__(WARPS * 32, MINB) gemv_int4_kernel(const XT *__restrict__ x,
                                                                const uint8_t *__restrict__ packed,
                                                                const float *__restrict__ scales,
-                                                               float *__restrict__ y, int m, int n, int k, int kp,
+                                                               OutSpec y, int m, int n, int k, int kp,
                                                                int gshift, int xstride, int prefetch) {
     static_assert(!SA || std::is_same<XT, __half>::value, "scale-after mode is for fp16 x");
     // Dynamic shared memory: the double-buffered cross-warp reduction, then
@@ -373,7 +373,7 @@ __global__ void __launch_bounds__(WARPS * 32, MINB) gemv_int4_kernel(const XT *_
                         const int g2 = ln >> 2, t2 = ln & 3;
                         const int row = row0 + g2 + (e >= 2 ? 8 : 0);
                         const int mb = 8 * j + 2 * t2 + (e & 1);
-                        if (row < n && mb < m) y[(size_t)mb * n + row] = v;
+                        if (row < n && mb < m) y.store((size_t)mb * n + row, row, v);
                     }
                     jj = 0;
                     ++ti;
@@ -414,7 +414,7 @@ struct TmaGemvLayout {
 template <typename XT, int NT, int CW, int CPW, bool SA, bool XS, bool STMA>
 __global__ void __launch_bounds__((CW + 1) * 32, CW <= 8 ? 2 : 1)
     gemv_tma_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap smap,
-                    const XT *__restrict__ x, const float *__restrict__ scales, float *__restrict__ y, int m, int n,
+                    const XT *__restrict__ x, const float *__restrict__ scales, OutSpec y, int m, int n,
                     int k, int kp, int gshift, int xstride, int nstages, int prefetch) {
     static_assert(!SA || std::is_same<XT, __half>::value, "scale-after mode is for fp16 x");
     using L = TmaGemvLayout<CW, CPW>;
@@ -587,7 +587,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW <= 8 ? 2 : 1)
                 const int g2 = ln >> 2, t2 = ln & 3;
                 const int row = row0 + g2 + (e >= 2 ? 8 : 0);
                 const int mb = 8 * j + 2 * t2 + (e & 1);
-                if (ok && row < n && mb < m) y[(size_t)mb * n + row] = v;
+                if (ok && row < n && mb < m) y.store((size_t)mb * n + row, row, v);
             }
             st = 0;
             ++ti;
@@ -608,7 +608,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW <= 8 ? 2 : 1)
 template <typename XT, int NT, bool SA, bool XS, bool STMA>
 __global__ void __launch_bounds__(256, 4)
     gemv_tile_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap smap,
-                     const XT *__restrict__ x, const float *__restrict__ scales, float *__restrict__ y, int m, int n,
+                     const XT *__restrict__ x, const float *__restrict__ scales, OutSpec y, int m, int n,
                      int k, int kp, int gshift, int xstride, int prefetch) {
     static_assert(!SA || std::is_same<XT, __half>::value, "scale-after mode is for fp16 x");
     constexpr int CW = 8, CPW = 4;
@@ -729,7 +729,7 @@ __global__ void __launch_bounds__(256, 4)
         const int g2 = ln >> 2, t2 = ln & 3;
         const int row = row0 + g2 + (e >= 2 ? 8 : 0);
         const int mb = 8 * j + 2 * t2 + (e & 1);
-        if (ok && row < n && mb < m) y[(size_t)mb * n + row] = v;
+        if (ok && row < n && mb < m) y.store((size_t)mb * n + row, row, v);
     }
 }
 
@@ -748,7 +748,7 @@ __global__ void __launch_bounds__(256, 4)
 template <typename XT, int NT, bool SA, bool XS, bool STMA>
 __global__ void __launch_bounds__(512, 2)
     gemv_pair_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap smap,
-                     const XT *__restrict__ x, const float *__restrict__ scales, float *__restrict__ y, int m, int n,
+                     const XT *__restrict__ x, const float *__restrict__ scales, OutSpec y, int m, int n,
                      int k, int kp, int gshift, int xstride, int prefetch) {
     static_assert(!SA || std::is_same<XT, __half>::value, "scale-after mode is for fp16 x");
     constexpr int CW = 8, CPW = 4;
@@ -878,7 +878,7 @@ __global__ void __launch_bounds__(512, 2)
         const int g2 = ln >> 2, t2 = ln & 3;
         const int row = row0 + g2 + (e >= 2 ? 8 : 0);
         const int mb = 8 * j + 2 * t2 + (e & 1);
-        if (ok && row < n && mb < m) y[(size_t)mb * n + row] = v;
+        if (ok && row < n && mb < m) y.store((size_t)mb * n + row, row, v);
     }
 }
 
@@ -888,7 +888,7 @@ __global__ void __launch_bounds__(512, 2)
 // over K, up to 8 batch rows per pass (more passes for larger M).
 template <typename XT>
 __global__ void __launch_bounds__(256) simt_int4_kernel(const XT *__restrict__ x, const uint8_t *__restrict__ packed,
-                                                        const float *__restrict__ scales, float *__restrict__ y,
+                                                        const float *__restrict__ scales, OutSpec y,
                                                         int64_t m, int64_t n, int64_t k, int64_t kp, int g) {
     const int lane = threadIdx.x & 31;
     const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
@@ -909,7 +909,7 @@ __global__ void __launch_bounds__(256) simt_int4_kernel(const XT *__restrict__ x
                 float v = acc[i];
 #pragma unroll
                 for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-                if (lane == 0 && m0 + i < m) y[(m0 + i) * n + row] = v;
+                if (lane == 0 && m0 + i < m) y.store((size_t)(m0 + i) * n + row, (int)row, v);
             }
         }
     }
@@ -950,7 +950,7 @@ inline int allow_max_smem(const void *kern) {
 // other kernel it behaves like a normal launch.
 template <typename Kern, typename XT>
 int launch_pdl(Kern kern, unsigned blocks, unsigned threads, size_t smem, cudaStream_t st, const XT *x,
-               const uint8_t *packed, const float *scales, float *y, int m, int n, int k, int kp, int gshift,
+               const uint8_t *packed, const float *scales, OutSpec y, int m, int n, int k, int kp, int gshift,
                int xstride, int prefetch) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(blocks);
@@ -980,7 +980,7 @@ inline size_t gemv_xs_bytes(int64_t m, int64_t kp, int xsize) {
 }
 
 template <typename XT, int NT, int WARPS, int U, int MINB, bool SA>
-int launch_gemv_t(const XT *x, const uint8_t *packed, const float *scales, float *y, int64_t m, int64_t n,
+int launch_gemv_t(const XT *x, const uint8_t *packed, const float *scales, OutSpec y, int64_t m, int64_t n,
                   int64_t k, int64_t kp, int gshift, int prefetch, cudaStream_t st) {
     // Persistent grid: MINB CTAs per SM, each looping over 16-row tiles.
     const int64_t tiles = cdiv(n, 16);
@@ -1048,7 +1048,7 @@ int make_gemv_maps(const uint8_t *packed, const float *scales, int64_t n, int64_
 }
 
 template <typename XT, int NT, int CW, int CPW, bool SA, int CTAS = 1>
-int launch_gemv_tma(const XT *x, const uint8_t *packed, const float *scales, float *y, int64_t m, int64_t n,
+int launch_gemv_tma(const XT *x, const uint8_t *packed, const float *scales, OutSpec y, int64_t m, int64_t n,
                     int64_t k, int64_t kp, int g, int gshift, int prefetch, cudaStream_t st) {
     using L = TmaGemvLayout<CW, CPW>;
     size_t smem = 0;
@@ -1103,7 +1103,7 @@ inline bool gemv_tile_ok(int64_t m, int64_t n, int64_t k, int64_t kp, int g, con
 }
 
 template <typename XT, int NT, bool SA>
-int launch_gemv_tile(const XT *x, const uint8_t *packed, const float *scales, float *y, int64_t m, int64_t n,
+int launch_gemv_tile(const XT *x, const uint8_t *packed, const float *scales, OutSpec y, int64_t m, int64_t n,
                      int64_t k, int64_t kp, int g, int gshift, int prefetch, cudaStream_t st) {
     using L = TmaGemvLayout<8, 4>;
     if (!gemv_tile_ok(m, n, k, kp, g, packed)) return invalid("tile GEMV (config 12) does not take this shape");
@@ -1149,7 +1149,7 @@ inline bool gemv_pair_ok(int64_t m, int64_t n, int64_t k, int64_t kp, int g, con
 }
 
 template <typename XT, int NT, bool SA>
-int launch_gemv_pair(const XT *x, const uint8_t *packed, const float *scales, float *y, int64_t m, int64_t n,
+int launch_gemv_pair(const XT *x, const uint8_t *packed, const float *scales, OutSpec y, int64_t m, int64_t n,
                      int64_t k, int64_t kp, int g, int gshift, int prefetch, cudaStream_t st) {
     using L = TmaGemvLayout<8, 4>;
     if (!gemv_pair_ok(m, n, k, kp, g, packed)) return invalid("pair GEMV (config 13) does not take this shape");
@@ -1225,7 +1225,7 @@ bool tma_gemv_ok(int64_t m, int64_t k, int64_t kp, int g, const uint8_t *packed)
 constexpr int kGemvConfigs = 13;
 
 template <typename XT, int NT, bool SA>
-int launch_gemv_nt(int config, const XT *x, const uint8_t *packed, const float *scales, float *y, int64_t m,
+int launch_gemv_nt(int config, const XT *x, const uint8_t *packed, const float *scales, OutSpec y, int64_t m,
                    int64_t n, int64_t k, int64_t kp, int g, int gshift, int pf, cudaStream_t st) {
     switch (config) {
         case 1: return launch_gemv_t<XT, NT, 8, 4, 2, SA>(x, packed, scales, y, m, n, k, kp, gshift, pf, st);
@@ -1255,7 +1255,7 @@ int launch_gemv_nt(int config, const XT *x, const uint8_t *packed, const float *
 }
 
 template <typename XT, bool SA>
-int launch_gemv_sa(int shape, const XT *x, const uint8_t *packed, const float *scales, float *y, int64_t m,
+int launch_gemv_sa(int shape, const XT *x, const uint8_t *packed, const float *scales, OutSpec y, int64_t m,
                    int64_t n, int64_t k, int64_t kp, int g, int gshift, int pf, cudaStream_t st) {
     switch ((m + 7) / 8) {
         case 1: return launch_gemv_nt<XT, 1, SA>(shape, x, packed, scales, y, m, n, k, kp, g, gshift, pf, st);
@@ -1266,7 +1266,7 @@ int launch_gemv_sa(int shape, const XT *x, const uint8_t *packed, const float *s
 }
 
 template <typename XT>
-int launch_gemv(const XT *x, const uint8_t *packed, const float *scales, float *y, int64_t m, int64_t n, int64_t k,
+int launch_gemv(const XT *x, const uint8_t *packed, const float *scales, OutSpec y, int64_t m, int64_t n, int64_t k,
                 int64_t kp, int g, int config, cudaStream_t st) {
     int gshift = 0;
     while ((1 << gshift) < g) ++gshift;
@@ -1301,7 +1301,7 @@ int launch_gemv(const XT *x, const uint8_t *packed, const float *scales, float *
 }
 
 template <typename XT>
-int launch_simt(const XT *x, const uint8_t *packed, const float *scales, float *y, int64_t m, int64_t n, int64_t k,
+int launch_simt(const XT *x, const uint8_t *packed, const float *scales, OutSpec y, int64_t m, int64_t n, int64_t k,
                 int64_t kp, int g, cudaStream_t st) {
     int64_t blocks = cdiv(n, 8);
     const int64_t cap = (int64_t)sm_count() * 8;
@@ -1326,14 +1326,16 @@ bool gemv_supported(int64_t m, int64_t n, int64_t k, int g, const void *x, const
 
 using namespace oq;
 
-extern "C" int oq_int4_linear(const void *x, int x_dtype, const uint8_t *packed, const float *scales, float *y,
-                              int64_t m, int64_t n, int64_t k, int group_size, int kernel, int config,
-                              oq_stream_t stream) {
-    clear_error();
+namespace oq {
+namespace {
+
+int int4_linear_impl(const void *x, int x_dtype, const uint8_t *packed, const float *scales, OutSpec y, int64_t m,
+                     int64_t n, int64_t k, int group_size, int kernel, int config, oq_stream_t stream) {
     OQ_REQUIRE(x_dtype == OQ_F16 || x_dtype == OQ_BF16, "Input must be a 2D FP16 or BF16 tensor");
     OQ_REQUIRE(group_size >= 2 && group_size % 2 == 0, "Group size must be even and >= 2");
     OQ_REQUIRE(m >= 1 && n >= 1 && k >= 1, "Matrix dimensions must be positive");
-    OQ_REQUIRE(x && packed && scales && y, "null pointer argument");
+    OQ_REQUIRE(x && packed && scales && y.y, "null pointer argument");
+    OQ_REQUIRE(y.dtype == OQ_F32 || y.dtype == OQ_F16 || y.dtype == OQ_BF16, "output dtype must be fp32, fp16 or bf16");
     const int64_t kp = cdiv(k, group_size) * group_size;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const bool gemv_ok = gemv_supported(m, n, k, group_size, x, packed);
@@ -1341,7 +1343,7 @@ extern "C" int oq_int4_linear(const void *x, int x_dtype, const uint8_t *packed,
     if (which == OQ_KERNEL_AUTO) {
         if (gemv_ok && m <= 16)
             which = OQ_KERNEL_GEMV;
-        else if (gemm_tcgen05_supported(m, n, k, group_size, x, packed, y))
+        else if (gemm_tcgen05_supported(m, n, k, group_size, x, packed, nullptr))
             which = OQ_KERNEL_TCGEN05;
         else if (gemv_ok)
             which = OQ_KERNEL_GEMV;
@@ -1357,7 +1359,7 @@ extern "C" int oq_int4_linear(const void *x, int x_dtype, const uint8_t *packed,
             return launch_gemv(static_cast<const __nv_bfloat16 *>(x), packed, scales, y, m, n, k, kp, group_size,
                                config, st);
         case OQ_KERNEL_TCGEN05:
-            OQ_REQUIRE(gemm_tcgen05_supported(m, n, k, group_size, x, packed, y),
+            OQ_REQUIRE(gemm_tcgen05_supported(m, n, k, group_size, x, packed, nullptr),
                        "tcgen05 kernel does not support this shape/alignment");
             return gemm_tcgen05_launch(x, x_dtype, packed, scales, y, m, n, k, group_size, st);
         case OQ_KERNEL_SIMT:
@@ -1367,4 +1369,23 @@ extern "C" int oq_int4_linear(const void *x, int x_dtype, const uint8_t *packed,
         default:
             return invalid("unknown kernel selector %d", kernel);
     }
+}
+
+}  // namespace
+}  // namespace oq
+
+extern "C" int oq_int4_linear(const void *x, int x_dtype, const uint8_t *packed, const float *scales, float *y,
+                              int64_t m, int64_t n, int64_t k, int group_size, int kernel, int config,
+                              oq_stream_t stream) {
+    clear_error();
+    return int4_linear_impl(x, x_dtype, packed, scales, OutSpec{y, nullptr, OQ_F32}, m, n, k, group_size, kernel,
+                            config, stream);
+}
+
+extern "C" int oq_int4_linear_ex(const void *x, int x_dtype, const uint8_t *packed, const float *scales, void *y,
+                                 int y_dtype, const float *bias, int64_t m, int64_t n, int64_t k, int group_size,
+                                 int kernel, int config, oq_stream_t stream) {
+    clear_error();
+    return int4_linear_impl(x, x_dtype, packed, scales, OutSpec{y, bias, y_dtype}, m, n, k, group_size, kernel,
+                            config, stream);
 }

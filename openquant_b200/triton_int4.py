@@ -18,7 +18,7 @@ __all__ = ["int4_linear"]
 
 
 def int4_linear(x, packed, scales, out_features, group_size, *, block_m=64, block_n=64, block_k=64, num_warps=4,
-                kernel=None, out=None, exact_rounding=False, static_weights=False):
+                kernel=None, out=None, exact_rounding=False, static_weights=False, bias=None, out_dtype=None):
     """y = x @ W^T in fp32, W[n, k] = round_x(int4(n, k) * scales[n, k // g]).
 
     Arguments and errors follow triton_int4.py:78-118 (ValueError for each
@@ -39,6 +39,12 @@ def int4_linear(x, packed, scales, out_features, group_size, *, block_m=64, bloc
     reference, and within the parity tolerance of it).  exact_rounding=True
     instead rounds every weight to fp16 as the reference kernel does, bit
     for bit; bf16 x and larger M always do.
+
+    bias (fp32 [N] on x's device) is added to every output row and out_dtype
+    (torch.float32 by default, or torch.float16 / torch.bfloat16) is the type
+    y is written in -- both fused into the kernel's epilogue: the bias is
+    added in fp32 and the sum rounded once.  With out= the output's dtype is
+    used.
 
     static_weights=True declares that `packed` and `scales` were written
     before any kernel still in flight on the stream (quantized at load time
@@ -76,11 +82,19 @@ def int4_linear(x, packed, scales, out_features, group_size, *, block_m=64, bloc
         if int(v) < 1:
             raise ValueError("Tile arguments must be positive")
 
+    ycodes = {torch.float32: nat.OQ_F32, torch.float16: nat.OQ_F16, torch.bfloat16: nat.OQ_BF16}
     if out is None:
-        out = torch.empty((m, n), device=x.device, dtype=torch.float32)
-    elif (out.shape != (m, n) or out.dtype != torch.float32 or out.device != x.device
-          or not out.is_contiguous()):
-        raise ValueError("out must be a contiguous float32 (M, N) tensor on x's device")
+        odt = torch.float32 if out_dtype is None else out_dtype
+        if odt not in ycodes:
+            raise ValueError("out_dtype must be torch.float32, torch.float16 or torch.bfloat16")
+        out = torch.empty((m, n), device=x.device, dtype=odt)
+    elif (out.shape != (m, n) or out.dtype not in ycodes or out.device != x.device or not out.is_contiguous()
+          or (out_dtype is not None and out.dtype != out_dtype)):
+        raise ValueError("out must be a contiguous float32, float16 or bfloat16 (M, N) tensor on x's device")
+    if bias is not None:
+        if (not isinstance(bias, torch.Tensor) or bias.dtype != torch.float32 or bias.numel() != n
+                or bias.device != x.device or not bias.is_contiguous()):
+            raise ValueError("bias must be a contiguous float32 tensor of N elements on x's device")
 
     nat.require_device()
     if kernel is None:
@@ -95,6 +109,11 @@ def int4_linear(x, packed, scales, out_features, group_size, *, block_m=64, bloc
         split |= nat.CONFIG_STATIC_WEIGHTS
     code = nat.OQ_F16 if x.dtype == torch.float16 else nat.OQ_BF16
     with torch.cuda.device(x.device):
-        nat.check(nat.load().oq_int4_linear(nat.ptr(x), code, nat.ptr(packed), nat.ptr(scales), nat.ptr(out),
-                                            m, n, k, g, sel, split, nat.stream_of(x.device)))
+        if bias is None and out.dtype == torch.float32:
+            nat.check(nat.load().oq_int4_linear(nat.ptr(x), code, nat.ptr(packed), nat.ptr(scales), nat.ptr(out),
+                                                m, n, k, g, sel, split, nat.stream_of(x.device)))
+        else:
+            nat.check(nat.load().oq_int4_linear_ex(nat.ptr(x), code, nat.ptr(packed), nat.ptr(scales), nat.ptr(out),
+                                                   ycodes[out.dtype], nat.ptr(bias) if bias is not None else None,
+                                                   m, n, k, g, sel, split, nat.stream_of(x.device)))
     return out

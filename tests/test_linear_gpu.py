@@ -323,3 +323,44 @@ def test_fp16_scale_after_vs_exact_rounding(shape):
         assert (fast - true).norm().item() < (exact - true).norm().item()
     else:  # M > 8 uses the exact rounding by default
         assert ((fast - exact).norm() / exact.norm()).item() < 1e-5
+
+
+@pytest.mark.parametrize("kernel", ["gemv", "simt", "tcgen05", None])
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("shape", [(1, 4096, 4096, 128), (5, 300, 1024, 64), (300, 640, 1024, 128)])
+def test_fused_bias_and_output_dtype(shape, out_dtype, kernel):
+    """The fused epilogue adds the bias in fp32 and rounds once, exactly as
+    (fp32 result + bias).to(dtype) does."""
+    from openquant.triton_int4 import int4_linear
+
+    m, n, k, g = shape
+    if kernel == "gemv" and m > 64:
+        pytest.skip("GEMV takes M <= 64")
+    x, q, xt = make_case(m, n, k, g, torch.float16, seed=m + n, w_sigma=0.02)
+    p, s = torch.from_numpy(q.data).cuda(), torch.from_numpy(q.scales).cuda()
+    bias = torch.randn(n, device="cuda")
+    y32 = int4_linear(xt, p, s, n, g, kernel=kernel)
+    y = int4_linear(xt, p, s, n, g, kernel=kernel, bias=bias, out_dtype=out_dtype)
+    assert y.dtype == out_dtype and y.shape == (m, n)
+    assert torch.equal(y, (y32 + bias).to(out_dtype))
+    out = torch.empty(m, n, dtype=out_dtype, device="cuda")
+    assert int4_linear(xt, p, s, n, g, kernel=kernel, bias=bias, out=out) is out
+    assert torch.equal(out, y)
+
+
+def test_fused_epilogue_every_gemv_config():
+    from openquant_b200 import _native as nat
+
+    m, n, k, g = 1, 4096, 4096, 128
+    x, q, xt = make_case(m, n, k, g, torch.float16, seed=9, w_sigma=0.02)
+    p, s = torch.from_numpy(q.data).cuda(), torch.from_numpy(q.scales).cuda()
+    bias = torch.randn(n, device="cuda")
+    lib = nat.load()
+    for cfg in (0, 1, 8, 9, 10, 12, 13, 13 | 32):
+        y32 = torch.empty(m, n, device="cuda")
+        nat.check(lib.oq_int4_linear(nat.ptr(xt), nat.OQ_F16, nat.ptr(p), nat.ptr(s), nat.ptr(y32), m, n, k, g, 1,
+                                     cfg, nat.stream_of(xt.device)))
+        yb = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+        nat.check(lib.oq_int4_linear_ex(nat.ptr(xt), nat.OQ_F16, nat.ptr(p), nat.ptr(s), nat.ptr(yb), nat.OQ_BF16,
+                                        nat.ptr(bias), m, n, k, g, 1, cfg, nat.stream_of(xt.device)))
+        assert torch.equal(yb, (y32 + bias).to(torch.bfloat16)), cfg
