@@ -81,6 +81,13 @@ typedef void *oq_stream_t; /* a cudaStream_t */
  * No counterpart in the reference (its Triton launch is stream-ordered). */
 #define OQ_CONFIG_STATIC_WEIGHTS 32
 
+/* oq_int4_linear / oq_int4_linear_ex `config` flag: SiLU-gate fusion of a
+ * gate/up pair.  packed and scales hold the [gate; up] stack -- 2n rows,
+ * gate rows first -- and y (M x n) = silu(x . Wg^T) * (x . Wu^T) with
+ * silu(g) = g / (1 + exp(-g)), in one GEMV pass (M <= 16, no bias).  No
+ * counterpart in the reference. */
+#define OQ_CONFIG_SILU_GATE 64
+
 /* Library version string ("openquant_b200 <x.y.z> sm_100a"). */
 OQ_API const char *oq_version(void);
 

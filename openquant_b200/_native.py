@@ -19,6 +19,7 @@ OQ_F32, OQ_F16, OQ_BF16, OQ_F64 = 0, 1, 2, 3
 KERNELS = {"auto": 0, "gemv": 1, "simt": 2, "tcgen05": 3}
 CONFIG_EXACT_ROUNDING = 16
 CONFIG_STATIC_WEIGHTS = 32
+CONFIG_SILU_GATE = 64
 
 # name -> (restype, argtypes), exactly the declarations of the header.
 _P, _I64, _I32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int

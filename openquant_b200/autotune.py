@@ -43,7 +43,7 @@ def candidates(m):
     """(name, kernel code, config) pairs worth trying at batch size m."""
     out = []
     if m <= 64:
-        shapes = range(1, 11) if m <= 16 else range(1, 8)
+        shapes = [*range(1, 11), 12, 13] if m <= 16 else range(1, 8)
         out += [(f"gemv:{c}", nat.KERNELS["gemv"], c) for c in shapes]
     out.append(("tcgen05", nat.KERNELS["tcgen05"], 0))
     if m <= 256:

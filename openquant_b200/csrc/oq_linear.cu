@@ -415,7 +415,7 @@ template <typename XT, int NT, int CW, int CPW, bool SA, bool XS, bool STMA>
 __global__ void __launch_bounds__((CW + 1) * 32, CW <= 8 ? 2 : 1)
     gemv_tma_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap smap,
                     const XT *__restrict__ x, const float *__restrict__ scales, OutSpec y, int m, int n,
-                    int k, int kp, int gshift, int xstride, int nstages, int prefetch) {
+                    int k, int kp, int gshift, int xstride, int nstages, int prefetch, int gate_n) {
     static_assert(!SA || std::is_same<XT, __half>::value, "scale-after mode is for fp16 x");
     using L = TmaGemvLayout<CW, CPW>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -432,8 +432,18 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW <= 8 ? 2 : 1)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int groups = kp >> gshift;
-    const int tiles = (n + 15) >> 4;
-    const int my_tiles = (int)blockIdx.x < tiles ? (tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    // gate_n > 0 (SiLU-gate mode): the weights are the [gate; up] stack of
+    // 2 gate_n rows; the CTA walks tile pairs u = blockIdx.x + j * gridDim.x,
+    // gate tile u (rows 16u..) then up tile u (rows gate_n + 16u..), and
+    // writes silu(gate) * up for the gate_n output features.
+    static_assert(NT * 4 * 32 <= CW * 32, "one reduced output per thread and tile");
+    const int units = gate_n ? (gate_n + 15) >> 4 : (n + 15) >> 4;
+    const int my_units = (int)blockIdx.x < units ? (units - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    const int my_tiles = gate_n ? 2 * my_units : my_units;
+    auto tile_row0 = [&](int ti) {
+        return gate_n ? ((ti & 1) ? gate_n : 0) + ((int)blockIdx.x + (ti >> 1) * (int)gridDim.x) * 16
+                      : ((int)blockIdx.x + ti * (int)gridDim.x) * 16;
+    };
     const int nchunks = (kp + 127) >> 7;
     const int spt = (kp + L::kStageCols - 1) / L::kStageCols;  // stages per tile
     const int npos = my_tiles * spt;
@@ -459,7 +469,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW <= 8 ? 2 : 1)
                 const int slot = pos % nstages, round = pos / nstages;
                 if (round > 0 && !mbar_wait(&empty[slot], (round - 1) & 1)) break;
                 const int ti = pos / spt, st = pos - ti * spt;
-                const int row0 = ((int)blockIdx.x + ti * (int)gridDim.x) * 16;
+                const int row0 = tile_row0(ti);
                 const int k0 = st * L::kStageCols;
                 mbar_arrive_expect_tx(&full[slot], L::kStageBytes + (STMA ? 16 * spr * 4 : 0));
 #pragma unroll
@@ -509,10 +519,11 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW <= 8 ? 2 : 1)
         for (int j = 0; j < NT; ++j) acc[a][j][0] = acc[a][j][1] = acc[a][j][2] = acc[a][j][3] = 0.0f;
 
     bool ok = true;
+    float gsave = 0.0f;  // SiLU-gate mode: this thread's reduced gate value
     int ti = 0, st = 0;
     for (int pos = 0; pos < npos; ++pos) {
         const int slot = pos % nstages, round = pos / nstages;
-        const int row0 = ((int)blockIdx.x + ti * (int)gridDim.x) * 16;
+        const int row0 = tile_row0(ti);
         // Scales without TMA: each lane reads its two rows' scales for its
         // chunks of this stage straight from global memory.
         float sreg[CPW][2];
@@ -587,7 +598,14 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW <= 8 ? 2 : 1)
                 const int g2 = ln >> 2, t2 = ln & 3;
                 const int row = row0 + g2 + (e >= 2 ? 8 : 0);
                 const int mb = 8 * j + 2 * t2 + (e & 1);
-                if (ok && row < n && mb < m) y.store((size_t)mb * n + row, row, v);
+                if (gate_n == 0) {
+                    if (ok && row < n && mb < m) y.store((size_t)mb * n + row, row, v);
+                } else if ((ti & 1) == 0) {
+                    gsave = v;  // gate tile: kept until the matching up tile
+                } else {
+                    const int f = row - gate_n;  // output feature
+                    if (ok && f < gate_n && mb < m) y.store((size_t)mb * gate_n + f, f, gsave / (1.0f + expf(-gsave)) * v);
+                }
             }
             st = 0;
             ++ti;
@@ -1049,14 +1067,15 @@ int make_gemv_maps(const uint8_t *packed, const float *scales, int64_t n, int64_
 
 template <typename XT, int NT, int CW, int CPW, bool SA, int CTAS = 1>
 int launch_gemv_tma(const XT *x, const uint8_t *packed, const float *scales, OutSpec y, int64_t m, int64_t n,
-                    int64_t k, int64_t kp, int g, int gshift, int prefetch, cudaStream_t st) {
+                    int64_t k, int64_t kp, int g, int gshift, int prefetch, cudaStream_t st, int64_t gate_n = 0) {
     using L = TmaGemvLayout<CW, CPW>;
     size_t smem = 0;
     int xstride = 0;
     bool xs = false;
-    const int64_t tiles = cdiv(n, 16);
-    const int64_t grid = std::min<int64_t>(tiles, (int64_t)sm_count() * CTAS);
-    const int64_t max_pos = cdiv(tiles, grid) * cdiv(kp, L::kStageCols);
+    // units: 16-row tiles, or (gate_n > 0) gate/up tile pairs
+    const int64_t units = gate_n ? cdiv(gate_n, 16) : cdiv(n, 16);
+    const int64_t grid = std::min<int64_t>(units, (int64_t)sm_count() * CTAS);
+    const int64_t max_pos = cdiv(units, grid) * (gate_n ? 2 : 1) * cdiv(kp, L::kStageCols);
     const int stages = tma_gemv_plan<CW, CPW>(m, k, kp, g, NT, (int)sizeof(XT), &smem, &xstride, &xs, CTAS, max_pos);
     if (stages == 0) return invalid("TMA GEMV: shape does not fit in shared memory");
     CUtensorMap wmap, smap;
@@ -1077,7 +1096,7 @@ int launch_gemv_tma(const XT *x, const uint8_t *packed, const float *scales, Out
         cfg.attrs = attr;
         cfg.numAttrs = 1;
         cudaError_t err = cudaLaunchKernelEx(&cfg, kern, wmap, smap, x, scales, y, (int)m, (int)n, (int)k, (int)kp,
-                                             gshift, xstride, stages, prefetch);
+                                             gshift, xstride, stages, prefetch, (int)gate_n);
         if (err != cudaSuccess) {
             set_error("int4_linear (TMA GEMV): launch failed: %s", cudaGetErrorString(err));
             return OQ_ERR_CUDA;
@@ -1300,6 +1319,51 @@ int launch_gemv(const XT *x, const uint8_t *packed, const float *scales, OutSpec
     return launch_gemv_sa<XT, false>(shape, x, packed, scales, y, m, n, k, kp, g, gshift, pf, st);
 }
 
+// SiLU-gate mode (OQ_CONFIG_SILU_GATE): the TMA GEMV over the [gate; up]
+// stack of 2 * n_out rows, y = silu(x . Wg^T) * (x . Wu^T).  The launch
+// shape is config's (8, 9 or 10) or, for 0, the first of 10 (M <= 8), 9, 8
+// that takes the shape.
+template <typename XT>
+int launch_gemv_gate(const XT *x, const uint8_t *packed, const float *scales, OutSpec y, int64_t m, int64_t n_out,
+                     int64_t k, int64_t kp, int g, int config, cudaStream_t st) {
+    int gshift = 0;
+    while ((1 << gshift) < g) ++gshift;
+    const int nt = (int)((m + 7) / 8);
+    if (nt > 2) return invalid("SiLU-gate GEMV needs M <= 16");
+    int shape = config & 15;
+    const bool auto_shape = shape == 0;
+    if (auto_shape) {
+        if (nt == 1 && tma_gemv_ok<8, 4, 2>(m, k, kp, g, packed))
+            shape = 10;
+        else if (tma_gemv_ok<16, 2>(m, k, kp, g, packed))
+            shape = 9;
+        else if (tma_gemv_ok<8, 4>(m, k, kp, g, packed))
+            shape = 8;
+    }
+    const bool fits = (shape == 8 && tma_gemv_ok<8, 4>(m, k, kp, g, packed)) ||
+                      (shape == 9 && tma_gemv_ok<16, 2>(m, k, kp, g, packed)) ||
+                      (shape == 10 && tma_gemv_ok<8, 4, 2>(m, k, kp, g, packed));
+    if (!fits) return invalid("SiLU-gate GEMV: the TMA GEMV (config 8, 9 or 10) does not take this shape");
+    const bool exact = (config & OQ_CONFIG_EXACT_ROUNDING) != 0 || (auto_shape && nt > 1);
+    const int pf = (config & OQ_CONFIG_STATIC_WEIGHTS) != 0;
+    const int64_t n2 = 2 * n_out;
+    auto go = [&](auto sa_tag) -> int {
+        constexpr bool SA = decltype(sa_tag)::value;
+        if (nt == 1) {
+            if (shape == 8) return launch_gemv_tma<XT, 1, 8, 4, SA>(x, packed, scales, y, m, n2, k, kp, g, gshift, pf, st, n_out);
+            if (shape == 9) return launch_gemv_tma<XT, 1, 16, 2, SA>(x, packed, scales, y, m, n2, k, kp, g, gshift, pf, st, n_out);
+            return launch_gemv_tma<XT, 1, 8, 4, SA, 2>(x, packed, scales, y, m, n2, k, kp, g, gshift, pf, st, n_out);
+        }
+        if (shape == 8) return launch_gemv_tma<XT, 2, 8, 4, SA>(x, packed, scales, y, m, n2, k, kp, g, gshift, pf, st, n_out);
+        if (shape == 9) return launch_gemv_tma<XT, 2, 16, 2, SA>(x, packed, scales, y, m, n2, k, kp, g, gshift, pf, st, n_out);
+        return launch_gemv_tma<XT, 2, 8, 4, SA, 2>(x, packed, scales, y, m, n2, k, kp, g, gshift, pf, st, n_out);
+    };
+    if constexpr (std::is_same<XT, __half>::value) {
+        if (!exact && g % 128 == 0) return go(std::true_type{});
+    }
+    return go(std::false_type{});
+}
+
 template <typename XT>
 int launch_simt(const XT *x, const uint8_t *packed, const float *scales, OutSpec y, int64_t m, int64_t n, int64_t k,
                 int64_t kp, int g, cudaStream_t st) {
@@ -1338,6 +1402,16 @@ int int4_linear_impl(const void *x, int x_dtype, const uint8_t *packed, const fl
     OQ_REQUIRE(y.dtype == OQ_F32 || y.dtype == OQ_F16 || y.dtype == OQ_BF16, "output dtype must be fp32, fp16 or bf16");
     const int64_t kp = cdiv(k, group_size) * group_size;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (config & OQ_CONFIG_SILU_GATE) {
+        OQ_REQUIRE(kernel == OQ_KERNEL_AUTO || kernel == OQ_KERNEL_GEMV, "SiLU-gate fusion runs on the GEMV kernel");
+        OQ_REQUIRE(y.bias == nullptr, "SiLU-gate fusion takes no bias");
+        OQ_REQUIRE(m <= 16 && gemv_supported(m, 2 * n, k, group_size, x, packed),
+                   "SiLU-gate fusion needs M <= 16 and a shape the GEMV takes");
+        if (x_dtype == OQ_F16)
+            return launch_gemv_gate(static_cast<const __half *>(x), packed, scales, y, m, n, k, kp, group_size, config, st);
+        return launch_gemv_gate(static_cast<const __nv_bfloat16 *>(x), packed, scales, y, m, n, k, kp, group_size,
+                                config, st);
+    }
     const bool gemv_ok = gemv_supported(m, n, k, group_size, x, packed);
     int which = kernel;
     if (which == OQ_KERNEL_AUTO) {

@@ -18,7 +18,8 @@ __all__ = ["int4_linear"]
 
 
 def int4_linear(x, packed, scales, out_features, group_size, *, block_m=64, block_n=64, block_k=64, num_warps=4,
-                kernel=None, out=None, exact_rounding=False, static_weights=False, bias=None, out_dtype=None):
+                kernel=None, out=None, exact_rounding=False, static_weights=False, bias=None, out_dtype=None,
+                silu_gate=False):
     """y = x @ W^T in fp32, W[n, k] = round_x(int4(n, k) * scales[n, k // g]).
 
     Arguments and errors follow triton_int4.py:78-118 (ValueError for each
@@ -46,6 +47,11 @@ def int4_linear(x, packed, scales, out_features, group_size, *, block_m=64, bloc
     added in fp32 and the sum rounded once.  With out= the output's dtype is
     used.
 
+    silu_gate=True fuses the gate/up pair of an MLP: `packed` and `scales`
+    hold the [gate; up] stack (2 * out_features rows, gate first) and y is
+    silu(x . Wg^T) * (x . Wu^T) with silu(g) = g / (1 + exp(-g)), computed in
+    one GEMV pass (M <= 16, no bias).
+
     static_weights=True declares that `packed` and `scales` were written
     before any kernel still in flight on the stream (quantized at load time
     and synchronized): the decode GEMV then streams them while the previous
@@ -70,10 +76,13 @@ def int4_linear(x, packed, scales, out_features, group_size, *, block_m=64, bloc
     groups = kp // g
     if m < 1 or n < 1 or k < 1:
         raise ValueError("Matrix dimensions must be positive")
-    if tuple(scales.shape) != (n, groups):
+    rows = 2 * n if silu_gate else n  # weight rows: the [gate; up] stack with silu_gate
+    if tuple(scales.shape) != (rows, groups):
         raise ValueError("Incorrect scales shape")
-    if packed.numel() != n * kp // 2:
+    if packed.numel() != rows * kp // 2:
         raise ValueError("Incorrect packed weight count")
+    if silu_gate and (bias is not None or m > 16):
+        raise ValueError("silu_gate takes no bias and needs M <= 16")
     if not packed.is_contiguous() or not scales.is_contiguous():
         raise ValueError("Weights and scales must be contiguous")
     if packed.device != x.device or scales.device != x.device:
@@ -97,7 +106,11 @@ def int4_linear(x, packed, scales, out_features, group_size, *, block_m=64, bloc
             raise ValueError("bias must be a contiguous float32 tensor of N elements on x's device")
 
     nat.require_device()
-    if kernel is None:
+    if silu_gate:
+        if kernel not in (None, "gemv"):
+            raise ValueError("silu_gate runs on the GEMV kernel")
+        sel, split = nat.KERNELS["gemv"], nat.CONFIG_SILU_GATE
+    elif kernel is None:
         sel, split = tile_table.lookup(m, n, k, g)
     else:
         if kernel not in nat.KERNELS:
@@ -109,7 +122,7 @@ def int4_linear(x, packed, scales, out_features, group_size, *, block_m=64, bloc
         split |= nat.CONFIG_STATIC_WEIGHTS
     code = nat.OQ_F16 if x.dtype == torch.float16 else nat.OQ_BF16
     with torch.cuda.device(x.device):
-        if bias is None and out.dtype == torch.float32:
+        if bias is None and out.dtype == torch.float32 and not silu_gate:
             nat.check(nat.load().oq_int4_linear(nat.ptr(x), code, nat.ptr(packed), nat.ptr(scales), nat.ptr(out),
                                                 m, n, k, g, sel, split, nat.stream_of(x.device)))
         else:

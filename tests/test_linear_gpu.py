@@ -364,3 +364,54 @@ def test_fused_epilogue_every_gemv_config():
         nat.check(lib.oq_int4_linear_ex(nat.ptr(xt), nat.OQ_F16, nat.ptr(p), nat.ptr(s), nat.ptr(yb), nat.OQ_BF16,
                                         nat.ptr(bias), m, n, k, g, 1, cfg, nat.stream_of(xt.device)))
         assert torch.equal(yb, (y32 + bias).to(torch.bfloat16)), cfg
+
+
+@pytest.mark.parametrize("shape", [(1, 4096, 4096, 128), (3, 11008, 4096, 128), (16, 1000, 2048, 64), (1, 24, 512, 32)])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_silu_gate_fusion_matches_two_products(shape, dtype):
+    """silu_gate over the [gate; up] stack equals silu(gate) * up from two
+    launches of the same GEMV config (identical sums; silu from the GPU's
+    expf vs torch's sigmoid in fp64: within a few ulp); the Python API's
+    automatic choice is that same config."""
+    from openquant.groupwise import quantize_int4_groupwise
+    from openquant.triton_int4 import int4_linear
+    from openquant_b200 import _native as nat
+
+    m, n, k, g = shape
+    gen = torch.Generator(device="cuda").manual_seed(n + k)
+    w = torch.randn(2 * n, k, device="cuda", generator=gen).mul_(0.02).to(dtype)
+    q = quantize_int4_groupwise(w, g)
+    x = torch.randn(m, k, device="cuda", generator=gen).to(dtype)
+    code = nat.OQ_F16 if dtype == torch.float16 else nat.OQ_BF16
+    lib = nat.load()
+    half = q.data.numel() // 2
+
+    def run(packed, scales, out_cols, cfg):
+        y = torch.empty(m, out_cols, device="cuda")
+        nat.check(lib.oq_int4_linear(nat.ptr(x), code, nat.ptr(packed), nat.ptr(scales), nat.ptr(y), m, out_cols, k,
+                                     g, 1, cfg, nat.stream_of(x.device)))
+        return y
+
+    # the automatic choice: the first of 10 (M <= 8), 9, 8 that takes the
+    # shape, exact rounding for M > 8
+    exact = 0 if m <= 8 else nat.CONFIG_EXACT_ROUNDING
+    for cfg in ([10, 9, 8] if m <= 8 else [9, 8]):
+        try:
+            gate = run(q.data[:half], q.scales[:n], n, cfg | exact)
+            break
+        except ValueError:
+            continue
+    else:
+        pytest.fail("no TMA GEMV config takes this shape")
+    cfg |= exact
+    up = run(q.data[half:], q.scales[n:], n, cfg)
+    fused = run(q.data, q.scales, n, cfg | nat.CONFIG_SILU_GATE)
+    ref = (gate.double() * torch.sigmoid(gate.double())) * up.double()
+    err = (fused.double() - ref).abs()
+    assert float((err - 2e-6 * ref.abs()).max()) <= 1e-6, float(err.max())
+    y = int4_linear(x, q.data, q.scales, n, g, silu_gate=True)
+    assert y.shape == (m, n) and torch.equal(y, fused)
+    yb = int4_linear(x, q.data, q.scales, n, g, silu_gate=True, out_dtype=torch.bfloat16)
+    assert torch.equal(yb, fused.to(torch.bfloat16))
+    with pytest.raises(ValueError):
+        int4_linear(x, q.data, q.scales, n, g, silu_gate=True, bias=torch.zeros(n, device="cuda"))
