@@ -328,6 +328,112 @@ def measure_gemm(dev, peaks, steps=10, warmup=3):
     }
 
 
+DECODE_LAYERS = [("qkv", 4096, 12288), ("o_proj", 4096, 4096), ("gate_up", 4096, 22016), ("down", 11008, 4096)]
+
+
+def measure_decode_layers(dev, peaks, ms_=(1, 4, 16), sets=3, steps=200, warmup=20):
+    """GB/s of the decode GEMV over the Llama-2-7B layer set (fused QKV
+    4096->12288, O 4096->4096, fused gate/up 4096->22016, down 11008->4096),
+    group 128, fp16 x ~ N(0,1), weights ~ N(0,0.02) seeded per layer, at
+    M = 1, 4 and 16.  A step runs the four layers back to back through
+    oq_int4_linear (automatic kernel choice, static weights); `sets` copies
+    of the whole layer set (3 x 107 MB, beyond L2) are rotated.  Each layer
+    is also timed alone (a graph of its own launches over the copies)."""
+    import ctypes
+
+    import torch
+
+    from openquant_b200 import _native as nat
+    from openquant_b200.groupwise import Groupwise4, dequantize_int4_groupwise, quantize_int4_groupwise
+
+    lib = nat.load()
+    g = 128
+    layers = []  # per layer: (name, k, n, [(packed, scales)] * sets, bytes of weights + scales)
+    for li, (name, k, n) in enumerate(DECODE_LAYERS):
+        copies = []
+        for s in range(sets):
+            gen = torch.Generator(device=dev).manual_seed(500 + 10 * li + s)
+            w = torch.randn(n, k, generator=gen, device=dev).mul_(0.02).half()
+            q = quantize_int4_groupwise(w, g)
+            del w
+            copies.append((q.data, q.scales))
+        layers.append((name, k, n, copies, n * k // 2 + n * (k // g) * 4))
+    stream = torch.cuda.Stream(device=dev)
+    out = {}
+    rel_worst = 0.0
+    launches = 0
+    for m in ms_:
+        gen = torch.Generator(device=dev).manual_seed(900 + m)
+        xs = [torch.randn(m, k, generator=gen, device=dev).half() for (_, k, _, _, _) in layers]
+        ys = [torch.empty(m, n, device=dev) for (_, _, n, _, _) in layers]
+        calls = [[(ctypes.c_void_p(xs[li].data_ptr()), nat.OQ_F16, ctypes.c_void_p(p.data_ptr()),
+                   ctypes.c_void_p(sc.data_ptr()), ctypes.c_void_p(ys[li].data_ptr()), m, n, k, g, 0,
+                   nat.CONFIG_STATIC_WEIGHTS) for (p, sc) in copies]
+                 for li, (_, k, n, copies, _) in enumerate(layers)]
+        io = [m * k * 2 + m * n * 4 for (_, k, n, _, _) in layers]
+
+        def timed(seq):
+            """µs for the launch sequence `seq` (oq_int4_linear argument
+            tuples) replayed as one CUDA graph, after an eager warm-up."""
+            def run(h, items):
+                for a in items:
+                    if lib.oq_int4_linear(*a, h) != 0:
+                        raise RuntimeError(nat.last_error())
+            with torch.cuda.stream(stream):
+                run(ctypes.c_void_p(stream.cuda_stream), seq[:warmup])
+            stream.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                run(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream), seq)
+            graph.replay()
+            torch.cuda.synchronize()
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(stream):
+                start.record(stream)
+                graph.replay()
+                end.record(stream)
+            torch.cuda.synchronize()
+            del graph
+            return start.elapsed_time(end) * 1e3
+
+        step_seq = [calls[li][s % sets] for s in range(steps) for li in range(len(layers))]
+        step_us = timed(step_seq) / steps
+        launches += len(step_seq)
+        step_bytes = sum(b for (*_, b) in layers) + sum(io)
+        per_layer = {}
+        for li, (name, k, n, _, wb) in enumerate(layers):
+            us = timed([calls[li][s % sets] for s in range(steps)]) / steps
+            launches += steps
+            gbs = (wb + io[li]) / us / 1e3
+            per_layer[f"{name}_{k}x{n}"] = {"us": us, "gbs": gbs, "frac": gbs / peaks["hbm_gbs"]}
+        # spot check: the O projection (weight copy 0, run once more) against
+        # the reference's dequantise-then-matmul
+        with torch.cuda.stream(stream):
+            nat.check(lib.oq_int4_linear(*calls[1][0], ctypes.c_void_p(stream.cuda_stream)))
+        stream.synchronize()
+        p, sc = layers[1][3][0]
+        wref = dequantize_int4_groupwise(Groupwise4(p, sc, (4096, 4096), g)).half().double()
+        yref = xs[1].double() @ wref.T
+        rel = ((ys[1].double() - yref).norm() / yref.norm()).item()
+        assert rel < 1e-3, rel
+        rel_worst = max(rel_worst, rel)
+        gbs = step_bytes / step_us / 1e3
+        out[str(m)] = {"us_per_step": step_us, "gbs": gbs, "frac": gbs / peaks["hbm_gbs"], "layers": per_layer}
+    del layers
+    return {
+        "metric": "INT4 decode GEMV GB/s over the Llama-2-7B layer set (QKV, O, gate/up, down)",
+        "workload": "int4_gemv_llama2_7b_layers_g128_fp16",
+        "value": out["1"]["gbs"] if "1" in out else None,
+        "unit": "GB/s",
+        "value_is": "M=1, one step = the four layers back to back; per-M and per-layer figures in by_m",
+        "by_m": out,
+        "l2": f"{sets} copies of the layer set rotated (> L2)",
+        "launch": "CUDA graph of back-to-back launches (programmatic dependent launch), static weights",
+        "gpu_launches": launches,
+        "check_rel_l2": rel_worst,
+    }
+
+
 def measure_w8a8(dev, peaks, steps=10, warmup=3):
     """TOPS of the W8A8 GEMM (per-token INT8 x, per-row INT8 W, tcgen05
     kind::i8) at M = 2048, (K, N) = (8192, 28672), two weight copies
@@ -822,6 +928,8 @@ def run_ours(args):
             line["also"] = [measure_gemm(dev, peaks), measure_w8a8(dev, peaks)]
         else:
             line["also"] = [measure_sharded_gemm(dev, world, rank, peaks)]
+    if world == 1 and not args.no_layers:
+        line.setdefault("also", []).append(measure_decode_layers(dev, peaks))
     if not args.no_bulk:
         line.setdefault("also", []).append(measure_bulk_quant(dev, world, rank, peaks, layers=args.bulk_layers))
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -844,6 +952,7 @@ def main(argv=None):
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gemm", action="store_true", help="skip the M=2048 prefill GEMM measurement")
     ap.add_argument("--no-bulk", action="store_true", help="skip the bulk-quantization (70B stack) measurement")
+    ap.add_argument("--no-layers", action="store_true", help="skip the Llama-2-7B decode layer-set measurement")
     ap.add_argument("--bulk-layers", type=int, default=BULK_LAYERS,
                     help="layers of the bulk-quantization stack (default 80; fewer for profiling)")
     args = ap.parse_args(argv)

@@ -429,6 +429,8 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW <= 8 ? 2 : 1)
     uint64_t *empty = full + nstages;
     auto red = reinterpret_cast<float(*)[CW][NT][4][32]>(empty + nstages);  // [2]
     XT *xs = reinterpret_cast<XT *>(reinterpret_cast<uint8_t *>(red) + gemv_red_bytes(CW, NT));
+    constexpr bool FOLD = SA && XS;  // bias-folded dequantization (gemv_chunk_sa)
+    float *corr = reinterpret_cast<float *>(xs + (size_t)m * xstride);  // [chunks][16]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int groups = kp >> gshift;
@@ -487,15 +489,8 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW <= 8 ? 2 : 1)
     // ------------------------------------------------------ consumers
     const int gi = lane >> 2, t = lane & 3;
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    if (XS) {  // x [m][k] -> xs [m][xstride], zero beyond k (SA: pair-permuted)
-        const int rowv = xstride / 8, kv = k / 8;
-        for (int i = threadIdx.x; i < m * rowv; i += CW * 32) {
-            const int r = i / rowv, c = i - r * rowv;
-            uint4 v = c < kv ? __ldg(reinterpret_cast<const uint4 *>(x) + (size_t)r * kv + c) : make_uint4(0, 0, 0, 0);
-            if (SA)
-                v = sa_perm_x(v);
-            reinterpret_cast<uint4 *>(xs)[i] = v;
-        }
+    if (XS) {
+        gemv_stage_x<XT, SA, FOLD>(x, xs, corr, m, k, kp, xstride, CW * 32);
         asm volatile("bar.sync 1, %0;" ::"r"(CW * 32) : "memory");
     }
     uint32_t xaddr[NT];
@@ -557,7 +552,8 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW <= 8 ? 2 : 1)
                 const uint32_t qa[4] = {wa.x, wa.y, wa.z, wa.w};
                 const uint32_t qb[4] = {wb.x, wb.y, wb.z, wb.w};
                 if constexpr (SA) {
-                    gemv_chunk_sa<NT, XS>(c, qa, qb, in ? sa : 0.0f, in ? sb : 0.0f, xaddr, xon, xg, xb, acc);
+                    gemv_chunk_sa<NT, XS, FOLD>(c, qa, qb, in ? sa : 0.0f, in ? sb : 0.0f, xaddr, xon, xg, xb, acc,
+                                                corr + c * 16 + 2 * t);
                 } else {
                     const DqScale dsa = make_dq_scale(in ? sa : 0.0f), dsb = make_dq_scale(in ? sb : 0.0f);
                     if (__all_sync(0xffffffffu, dsa.fast && dsb.fast))
@@ -1029,8 +1025,11 @@ inline int tma_gemv_plan(int64_t m, int64_t k, int64_t kp, int g, int nt, int xs
     const size_t per_stage = (size_t)L::kStageBytes + sbytes + 16;
     const size_t cap = (size_t)max_smem_optin() / ctas_per_sm - (ctas_per_sm > 1 ? 1024 : 0);
     const size_t base = 1024 + gemv_red_bytes(CW, nt);
-    const size_t xbytes = (size_t)(m * xstride * xsize);
-    bool xs = base + xbytes + 3 * per_stage <= cap;
+    // Staged x (and, for the scale-after path, its bias table: gemv_stage_x)
+    // is worth a stage: reading x from global memory in every chunk costs
+    // more than the third stage hides.
+    const size_t xbytes = (size_t)(m * xstride * xsize) + (size_t)cdiv(kp, 128) * 16 * 4;
+    bool xs = base + xbytes + 2 * per_stage <= cap;
     if (!xs && !(kp == k && kp % L::kStageCols == 0)) return 0;
     const size_t fixed = base + (xs ? xbytes : 0);
     if (fixed + 2 * per_stage > cap) return 0;
@@ -1295,7 +1294,7 @@ int launch_gemv(const XT *x, const uint8_t *packed, const float *scales, OutSpec
     if (auto_shape) {
         if (gemv_pair_ok(m, n, k, kp, g, packed))
             shape = 13;
-        else if (nt == 1 && tma_gemv_ok<8, 4, 2>(m, k, kp, g, packed))
+        else if (nt == 1 && kp <= TmaGemvLayout<8, 4>::kStageCols && tma_gemv_ok<8, 4, 2>(m, k, kp, g, packed))
             shape = 10;
         else if (tma_gemv_ok<16, 2>(m, k, kp, g, packed))
             shape = 9;
@@ -1321,7 +1320,7 @@ int launch_gemv(const XT *x, const uint8_t *packed, const float *scales, OutSpec
 
 // SiLU-gate mode (OQ_CONFIG_SILU_GATE): the TMA GEMV over the [gate; up]
 // stack of 2 * n_out rows, y = silu(x . Wg^T) * (x . Wu^T).  The launch
-// shape is config's (8, 9 or 10) or, for 0, the first of 10 (M <= 8), 9, 8
+// shape is config's (8, 9 or 10) or, for 0, the first of 10 (M <= 8, KP <= 4096), 9, 8
 // that takes the shape.
 template <typename XT>
 int launch_gemv_gate(const XT *x, const uint8_t *packed, const float *scales, OutSpec y, int64_t m, int64_t n_out,
@@ -1333,7 +1332,7 @@ int launch_gemv_gate(const XT *x, const uint8_t *packed, const float *scales, Ou
     int shape = config & 15;
     const bool auto_shape = shape == 0;
     if (auto_shape) {
-        if (nt == 1 && tma_gemv_ok<8, 4, 2>(m, k, kp, g, packed))
+        if (nt == 1 && kp <= TmaGemvLayout<8, 4>::kStageCols && tma_gemv_ok<8, 4, 2>(m, k, kp, g, packed))
             shape = 10;
         else if (tma_gemv_ok<16, 2>(m, k, kp, g, packed))
             shape = 9;
