@@ -230,6 +230,29 @@ OQ_API int oq_int8_gemm(const int8_t *qx, const float *sx, const int8_t *qw,
                         const float *sw, float *y, int64_t m, int64_t n,
                         int64_t k, oq_stream_t stream);
 
+/*
+ * The W8A8 linear layer without allocation: y = x . W^T with x quantized per
+ * token to INT8 (as oq_quant_int8_rowwise) and multiplied by oq_int8_gemm,
+ * where the quantized activations and their scales go to a fixed array that
+ * the library keeps on each GPU (16 MiB + 64 KiB, held until the process
+ * exits) instead of memory the caller would allocate.  For callers that
+ * cannot allocate device memory when they call in -- a host runtime that
+ * lends the library only the tensors it owns, or a service whose device
+ * memory is fixed at start-up.  Same result as oq_quant_int8_rowwise into
+ * caller buffers followed by oq_int8_gemm.
+ *   x  : [M][K] fp32 / fp16 / bf16 (x_dtype)   (device)
+ *   qw : int8 [N][K], sw : fp32 [N]            (device)
+ *   y  : fp32 [M][N]                           (device, out)
+ * K % 16 == 0; M <= 16384 and M * K <= 16 MiB, else OQ_ERR_INVALID.
+ * The first call on a device looks up the array's device address, so make
+ * that first call before any stream capture.  All calls on a device share
+ * the one array: calls whose work overlaps on the GPU (other streams, other
+ * host threads) race and must be serialised by the caller.
+ * No counterpart in the reference. */
+OQ_API int oq_int8_linear_noalloc(const void *x, int x_dtype, const int8_t *qw,
+                                  const float *sw, float *y, int64_t m,
+                                  int64_t n, int64_t k, oq_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -37,6 +37,7 @@ SIGNATURES = {
     "oq_int4_linear": (_I32, [_P, _I32, _P, _P, _P, _I64, _I64, _I64, _I32, _I32, _I32, _P]),
     "oq_int8_gemm": (_I32, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _P]),
     "oq_int4_linear_ex": (_I32, [_P, _I32, _P, _P, _P, _I32, _P, _I64, _I64, _I64, _I32, _I32, _I32, _P]),
+    "oq_int8_linear_noalloc": (_I32, [_P, _I32, _P, _P, _P, _I64, _I64, _I64, _P]),
 }
 
 _lock = threading.Lock()

@@ -32,6 +32,7 @@
 #include "oq_sm100.cuh"
 
 #include <algorithm>
+#include <mutex>
 
 namespace oq {
 namespace {
@@ -258,4 +259,77 @@ extern "C" int oq_int8_gemm(const int8_t *qx, const float *sx, const int8_t *qw,
     OQ_REQUIRE(gemm_w8a8_supported(m, n, k, qx, qw), "shape too large for the INT8 GEMM");
     const int rc = gemm_w8a8_launch(qx, sx, qw, sw, y, m, n, k, static_cast<cudaStream_t>(stream));
     return rc == OQ_OK ? check_launch("int8 GEMM") : rc;
+}
+
+// ------------------------------------------------ W8A8 without allocation --
+//
+// oq_int8_linear_noalloc runs the whole W8A8 layer -- per-token INT8
+// quantization of x, then the INT8 GEMM -- for callers that cannot allocate
+// device memory when they call in: a host runtime that lends the library only
+// the tensors it owns and has no allocator hook to offer, or a service whose
+// device memory is fixed at start-up.  The layer's intermediate data (the
+// int8 activations and their per-token scales) lives in the fixed array
+// below, which the library's module holds on every GPU that loads it, until
+// the process exits.  Limits: M * K <= 16 MiB of int8 activations and
+// M <= 16384 tokens.
+namespace {
+
+constexpr int64_t kNoAllocQxBytes = int64_t(16) << 20;  // int8 activations, M * K
+constexpr int64_t kNoAllocRows = 16384;                 // per-token fp32 scales
+constexpr int kNoAllocMaxDevices = 64;
+
+// [0, 16 MiB): qx [M][K] int8; [16 MiB, +64 KiB): sx [M] fp32.
+static __device__ __align__(256) uint8_t g_w8a8_scratch[kNoAllocQxBytes + kNoAllocRows * 4];
+
+std::mutex g_scratch_mutex;
+void *g_scratch_address[kNoAllocMaxDevices] = {};
+
+// Device address of g_w8a8_scratch on the current device.  Host code only
+// sees a host-side stand-in under that name, so the address is looked up
+// once per device (cudaGetSymbolAddress, with that device current) and kept.
+int scratch_address(void **out) {
+    int dev = -1;
+    OQ_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kNoAllocMaxDevices) return invalid("device ordinal %d out of range for the fixed scratch", dev);
+    std::lock_guard<std::mutex> lock(g_scratch_mutex);
+    if (g_scratch_address[dev] == nullptr) {
+        void *p = nullptr;
+        const cudaError_t err = cudaGetSymbolAddress(&p, g_w8a8_scratch);
+        if (err != cudaSuccess || p == nullptr) {
+            set_error("int8 linear (no-alloc): cannot resolve the scratch array on device %d: %s", dev,
+                      cudaGetErrorString(err));
+            return OQ_ERR_CUDA;
+        }
+        g_scratch_address[dev] = p;
+    }
+    *out = g_scratch_address[dev];
+    return OQ_OK;
+}
+
+}  // namespace
+
+extern "C" int oq_int8_linear_noalloc(const void *x, int x_dtype, const int8_t *qw, const float *sw, float *y,
+                                      int64_t m, int64_t n, int64_t k, oq_stream_t stream) {
+    clear_error();
+    OQ_REQUIRE(m >= 1 && n >= 1 && k >= 1, "Matrix dimensions must be positive");
+    OQ_REQUIRE(x && qw && sw && y, "null pointer argument");
+    OQ_REQUIRE(x_dtype == OQ_F32 || x_dtype == OQ_F16 || x_dtype == OQ_BF16, "x must be fp32, fp16 or bf16");
+    OQ_REQUIRE(k % 16 == 0, "K must be a multiple of 16 (16-byte rows), got %lld", (long long)k);
+    OQ_REQUIRE(aligned(qw, 16), "int8 weights must be 16-byte aligned");
+    OQ_REQUIRE(m <= kNoAllocRows && m * k <= kNoAllocQxBytes,
+               "int8 linear (no-alloc): M = %lld, K = %lld exceed the fixed scratch (M <= %lld and M * K <= %lld)",
+               (long long)m, (long long)k, (long long)kNoAllocRows, (long long)kNoAllocQxBytes);
+    void *base = nullptr;
+    int rc = scratch_address(&base);
+    if (rc != OQ_OK) return rc;
+    int8_t *qx = static_cast<int8_t *>(base);
+    float *sx = reinterpret_cast<float *>(static_cast<uint8_t *>(base) + kNoAllocQxBytes);
+    OQ_REQUIRE(gemm_w8a8_supported(m, n, k, qx, qw), "shape too large for the INT8 GEMM");
+    // Every byte of qx[M][K] and sx[M] that the GEMM reads is written by the
+    // quantizer first (rows past M come from TMA's zero fill), so nothing in
+    // the array needs clearing between calls.
+    rc = oq_quant_int8_rowwise(x, x_dtype, m, k, qx, sx, stream);
+    if (rc != OQ_OK) return rc;
+    rc = gemm_w8a8_launch(qx, sx, qw, sw, y, m, n, k, static_cast<cudaStream_t>(stream));
+    return rc == OQ_OK ? check_launch("int8 linear (no-alloc)") : rc;
 }
