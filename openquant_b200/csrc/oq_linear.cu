@@ -415,7 +415,7 @@ template <typename XT, int NT, int CW, int CPW, bool SA, bool XS, bool STMA>
 __global__ void __launch_bounds__((CW + 1) * 32, CW <= 8 ? 2 : 1)
     gemv_tma_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap smap,
                     const XT *__restrict__ x, const float *__restrict__ scales, OutSpec y, int m, int n,
-                    int k, int kp, int gshift, int xstride, int nstages, int prefetch, int gate_n) {
+                    int k, int kp, int gshift, int xstride, int nstages, int prefetch, int gate_n, int nred) {
     static_assert(!SA || std::is_same<XT, __half>::value, "scale-after mode is for fp16 x");
     using L = TmaGemvLayout<CW, CPW>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -427,8 +427,8 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW <= 8 ? 2 : 1)
     float *sbuf = reinterpret_cast<float *>(wbuf + (size_t)nstages * L::kStageBytes);  // [S][16][spr]
     uint64_t *full = reinterpret_cast<uint64_t *>(reinterpret_cast<uint8_t *>(sbuf) + (size_t)nstages * sbytes);
     uint64_t *empty = full + nstages;
-    auto red = reinterpret_cast<float(*)[CW][NT][4][32]>(empty + nstages);  // [2]
-    XT *xs = reinterpret_cast<XT *>(reinterpret_cast<uint8_t *>(red) + gemv_red_bytes(CW, NT));
+    auto red = reinterpret_cast<float(*)[CW][NT][4][32]>(empty + nstages);  // [nred]
+    XT *xs = reinterpret_cast<XT *>(reinterpret_cast<uint8_t *>(red) + gemv_red_bytes(CW, NT) / 2 * nred);
     constexpr bool FOLD = SA && XS;  // bias-folded dequantization (gemv_chunk_sa)
     float *corr = reinterpret_cast<float *>(xs + (size_t)m * xstride);  // [chunks][16]
 
@@ -576,7 +576,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW <= 8 ? 2 : 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[slot]);
         if (++st == spt) {
-            const int buf = ti & 1;
+            const int buf = nred == 2 ? (ti & 1) : 0;
 #pragma unroll
             for (int j = 0; j < NT; ++j)
 #pragma unroll
@@ -603,6 +603,9 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW <= 8 ? 2 : 1)
                     if (ok && f < gate_n && mb < m) y.store((size_t)mb * gate_n + f, f, gsave / (1.0f + expf(-gsave)) * v);
                 }
             }
+            // One reduction slot: every read of it ends before the next
+            // tile's partial sums are written.
+            if (nred == 1) asm volatile("bar.sync 1, %0;" ::"r"(CW * 32) : "memory");
             st = 0;
             ++ti;
         }
@@ -1011,12 +1014,17 @@ int launch_gemv_t(const XT *x, const uint8_t *packed, const float *scales, OutSp
 }
 
 // Stage count and shared-memory bytes of the TMA GEMV, or 0 stages when the
-// shape does not fit.  x is staged in shared memory when that leaves at
-// least 4 stages (*xs_out = 1), else read from global memory, which needs
-// whole stages (KP a multiple of the stage width and K == KP).
+// shape does not fit.  x (and, for the scale-after path, its bias table:
+// gemv_stage_x) is staged in shared memory whenever two stages still fit
+// (*xs_out = 1): reading x from global memory in every chunk costs more than
+// further stages hide.  To make room for a large x (M = 16) the cross-warp
+// reduction buffer drops from two tile slots to one (*nred_out = 1; the
+// kernel then takes one more barrier per tile).  Without staged x the stages
+// must be whole (KP a multiple of the stage width and K == KP).
 template <int CW, int CPW>
 inline int tma_gemv_plan(int64_t m, int64_t k, int64_t kp, int g, int nt, int xsize, size_t *smem_out,
-                         int *xstride_out, bool *xs_out, int ctas_per_sm = 1, int64_t max_pos = 1 << 30) {
+                         int *xstride_out, bool *xs_out, int *nred_out, int ctas_per_sm = 1,
+                         int64_t max_pos = 1 << 30) {
     using L = TmaGemvLayout<CW, CPW>;
     if (g < 32 || g > L::kStageCols) return 0;
     const int64_t xstride = cdiv(kp, 128) * 128 + 8;  // chunks past KP are skipped
@@ -1024,20 +1032,20 @@ inline int tma_gemv_plan(int64_t m, int64_t k, int64_t kp, int g, int nt, int xs
     const size_t sbytes = (size_t)cdiv(16 * spr * 4, 128) * 128;
     const size_t per_stage = (size_t)L::kStageBytes + sbytes + 16;
     const size_t cap = (size_t)max_smem_optin() / ctas_per_sm - (ctas_per_sm > 1 ? 1024 : 0);
-    const size_t base = 1024 + gemv_red_bytes(CW, nt);
-    // Staged x (and, for the scale-after path, its bias table: gemv_stage_x)
-    // is worth a stage: reading x from global memory in every chunk costs
-    // more than the third stage hides.
+    const size_t red2 = gemv_red_bytes(CW, nt);  // two tile slots
     const size_t xbytes = (size_t)(m * xstride * xsize) + (size_t)cdiv(kp, 128) * 16 * 4;
-    bool xs = base + xbytes + 2 * per_stage <= cap;
+    int nred = 2;
+    bool xs = 1024 + red2 + xbytes + 2 * per_stage <= cap;
+    if (!xs && 1024 + red2 / 2 + xbytes + 2 * per_stage <= cap) xs = true, nred = 1;
     if (!xs && !(kp == k && kp % L::kStageCols == 0)) return 0;
-    const size_t fixed = base + (xs ? xbytes : 0);
+    const size_t fixed = 1024 + red2 / 2 * nred + (xs ? xbytes : 0);
     if (fixed + 2 * per_stage > cap) return 0;
     int stages = (int)std::min<size_t>(8, (cap - fixed) / per_stage);
     stages = (int)std::max<int64_t>(2, std::min<int64_t>(stages, max_pos));
     *smem_out = fixed + stages * per_stage;
     *xstride_out = (int)xstride;
     *xs_out = xs;
+    *nred_out = nred;
     return stages;
 }
 
@@ -1075,7 +1083,9 @@ int launch_gemv_tma(const XT *x, const uint8_t *packed, const float *scales, Out
     const int64_t units = gate_n ? cdiv(gate_n, 16) : cdiv(n, 16);
     const int64_t grid = std::min<int64_t>(units, (int64_t)sm_count() * CTAS);
     const int64_t max_pos = cdiv(units, grid) * (gate_n ? 2 : 1) * cdiv(kp, L::kStageCols);
-    const int stages = tma_gemv_plan<CW, CPW>(m, k, kp, g, NT, (int)sizeof(XT), &smem, &xstride, &xs, CTAS, max_pos);
+    int nred = 2;
+    const int stages =
+        tma_gemv_plan<CW, CPW>(m, k, kp, g, NT, (int)sizeof(XT), &smem, &xstride, &xs, &nred, CTAS, max_pos);
     if (stages == 0) return invalid("TMA GEMV: shape does not fit in shared memory");
     CUtensorMap wmap, smap;
     bool stma = false;
@@ -1095,7 +1105,7 @@ int launch_gemv_tma(const XT *x, const uint8_t *packed, const float *scales, Out
         cfg.attrs = attr;
         cfg.numAttrs = 1;
         cudaError_t err = cudaLaunchKernelEx(&cfg, kern, wmap, smap, x, scales, y, (int)m, (int)n, (int)k, (int)kp,
-                                             gshift, xstride, stages, prefetch, (int)gate_n);
+                                             gshift, xstride, stages, prefetch, (int)gate_n, nred);
         if (err != cudaSuccess) {
             set_error("int4_linear (TMA GEMV): launch failed: %s", cudaGetErrorString(err));
             return OQ_ERR_CUDA;
@@ -1217,8 +1227,9 @@ bool tma_gemv_ok(int64_t m, int64_t k, int64_t kp, int g, const uint8_t *packed)
     size_t smem = 0;
     int xstride = 0;
     bool xs = false;
+    int nred = 2;
     return m <= 16 && aligned(packed, 16) && (kp / 2) % 16 == 0 &&
-           tma_gemv_plan<CW, CPW>(m, k, kp, g, (int)((m + 7) / 8), 2, &smem, &xstride, &xs, CTAS) > 0;
+           tma_gemv_plan<CW, CPW>(m, k, kp, g, (int)((m + 7) / 8), 2, &smem, &xstride, &xs, &nred, CTAS) > 0;
 }
 
 // GEMV launch shapes, selected by the low bits of oq_int4_linear's
