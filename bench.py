@@ -271,6 +271,7 @@ def measure_gemm(dev, peaks, steps=10, warmup=3):
     x = torch.randn(m, k, generator=gen, device=dev).to(torch.bfloat16)
     y = torch.empty(m, n, device=dev)
     stream = torch.cuda.Stream(device=dev)
+    torch.cuda.synchronize()  # inputs made on the default stream, launches on `stream`
 
     def launch(count, h):
         for i in range(count):
@@ -328,6 +329,89 @@ def measure_gemm(dev, peaks, steps=10, warmup=3):
     }
 
 
+PREFILL_SHAPES = [("gate_up", 8192, 28672), ("down", 28672, 8192)]
+
+
+def measure_prefill_set(dev, peaks, ms_=(512, 2048, 8192), steps=5, warmup=2):
+    """TFLOP/s of the prefill GEMM on the Llama-3-70B MLP shapes (gate/up
+    8192->28672, down 28672->8192), bf16 x ~ N(0,1), weights ~ N(0,0.02)
+    group 128, at M = 512, 2048 and 8192; two weight copies alternate (each
+    beyond L2), CUDA-graph replay, CUDA events.  Each case is checked on
+    sampled weight rows against the exactly-rounded weights."""
+    import ctypes
+
+    import torch
+
+    from oq_oracle import dequantize_int4_groupwise as deq, round_to_dtype
+    from openquant_b200 import _native as nat
+    from openquant_b200.groupwise import quantize_int4_groupwise
+
+    lib = nat.load()
+    g = 128
+    stream = torch.cuda.Stream(device=dev)
+    cases, rel_worst, launches = {}, 0.0, 0
+    for si, (name, k, n) in enumerate(PREFILL_SHAPES):
+        gen = torch.Generator(device=dev).manual_seed(700 + si)
+        w = torch.randn(n, k, generator=gen, device=dev).mul_(0.02).to(torch.bfloat16)
+        q = quantize_int4_groupwise(w, g)
+        del w
+        packs, scs = [q.data, q.data.clone()], [q.scales, q.scales.clone()]
+        rows = torch.arange(0, n, 1021, device=dev)
+        wr = torch.from_numpy(round_to_dtype(deq(q.data.view(n, k // 2)[rows].cpu().numpy().reshape(-1),
+                                                 q.scales[rows].cpu().numpy(), (len(rows), k), g), "bf16")).to(dev)
+        for m in ms_:
+            x = torch.randn(m, k, generator=gen, device=dev).to(torch.bfloat16)
+            y = torch.empty(m, n, device=dev)
+            torch.cuda.synchronize()  # inputs made on the default stream, launches on `stream`
+
+            def launch(count, h):
+                for i in range(count):
+                    st = lib.oq_int4_linear(ctypes.c_void_p(x.data_ptr()), nat.OQ_BF16,
+                                            ctypes.c_void_p(packs[i % 2].data_ptr()),
+                                            ctypes.c_void_p(scs[i % 2].data_ptr()), ctypes.c_void_p(y.data_ptr()),
+                                            m, n, k, g, 0, 0, h)
+                    if st != 0:
+                        raise RuntimeError(nat.last_error())
+
+            with torch.cuda.stream(stream):
+                launch(warmup, ctypes.c_void_p(stream.cuda_stream))
+            stream.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                launch(steps, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+            graph.replay()
+            torch.cuda.synchronize()
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(stream):
+                start.record(stream)
+                graph.replay()
+                end.record(stream)
+            torch.cuda.synchronize()
+            del graph
+            launches += warmup + 2 * steps
+            ms = start.elapsed_time(end) / steps
+            tflops = 2.0 * m * n * k / (ms / 1e3) / 1e12
+            ref = x.double() @ wr.double().T
+            rel = ((y[:, rows].double() - ref).norm() / ref.norm()).item()
+            assert rel < 1e-3, (name, m, rel)
+            rel_worst = max(rel_worst, rel)
+            cases[f"{name}_m{m}_k{k}_n{n}"] = {"ms": ms, "tflops": tflops, "frac": tflops / peaks["bf16_tflops"],
+                                              "frac_of_sustained": tflops / peaks["bf16_tflops_sustained"]}
+            del x, y
+        del packs, scs, q
+        torch.cuda.empty_cache()
+    return {
+        "metric": "INT4 dequant-GEMM TFLOP/s over the Llama-3-70B MLP prefill set",
+        "workload": "int4_gemm_llama3_70b_mlp_g128_bf16",
+        "value": cases[f"gate_up_m2048_k8192_n28672"]["tflops"] if 2048 in ms_ else None,
+        "unit": "TFLOP/s",
+        "value_is": "gate/up at M=2048; every (shape, M) case in by_case",
+        "by_case": cases,
+        "gpu_launches": launches,
+        "check_rel_l2": rel_worst,
+    }
+
+
 DECODE_LAYERS = [("qkv", 4096, 12288), ("o_proj", 4096, 4096), ("gate_up", 4096, 22016), ("down", 11008, 4096)]
 
 
@@ -366,6 +450,7 @@ def measure_decode_layers(dev, peaks, ms_=(1, 4, 16), sets=3, steps=200, warmup=
         gen = torch.Generator(device=dev).manual_seed(900 + m)
         xs = [torch.randn(m, k, generator=gen, device=dev).half() for (_, k, _, _, _) in layers]
         ys = [torch.empty(m, n, device=dev) for (_, _, n, _, _) in layers]
+        torch.cuda.synchronize()  # inputs made on the default stream, launches on `stream`
         calls = [[(ctypes.c_void_p(xs[li].data_ptr()), nat.OQ_F16, ctypes.c_void_p(p.data_ptr()),
                    ctypes.c_void_p(sc.data_ptr()), ctypes.c_void_p(ys[li].data_ptr()), m, n, k, g, 0,
                    nat.CONFIG_STATIC_WEIGHTS) for (p, sc) in copies]
@@ -455,6 +540,7 @@ def measure_w8a8(dev, peaks, steps=10, warmup=3):
     sx = torch.rand(m, generator=gen, device=dev) * 0.01 + 1e-3
     y = torch.empty(m, n, device=dev)
     stream = torch.cuda.Stream(device=dev)
+    torch.cuda.synchronize()  # inputs made on the default stream, launches on `stream`
 
     def launch(count, h):
         for i in range(count):
@@ -930,6 +1016,8 @@ def run_ours(args):
             line["also"] = [measure_sharded_gemm(dev, world, rank, peaks)]
     if world == 1 and not args.no_layers:
         line.setdefault("also", []).append(measure_decode_layers(dev, peaks))
+        if not args.no_gemm:
+            line["also"].append(measure_prefill_set(dev, peaks))
     if not args.no_bulk:
         line.setdefault("also", []).append(measure_bulk_quant(dev, world, rank, peaks, layers=args.bulk_layers))
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

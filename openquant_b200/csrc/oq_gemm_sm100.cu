@@ -11,17 +11,18 @@
 //   producer  : warp 0 -- TMA of the x tile (256 x 64, 128-byte swizzle) and
 //               of the packed weight tile (128 rows x 32 bytes) per k-block
 //               into a 4-stage shared-memory ring (full[s])
-//   dequant   : warps 4..7 -- thread r owns weight row r of the tile: it
-//               reads its 32 packed bytes, forms 64 exactly-rounded 16-bit
+//   dequant   : warps 8..8+4*kDqSplit-1 -- warp 8 + 4p + q serves TMEM
+//               lane quarter q: its thread for weight row r reads part p of
+//               the row's 32 packed bytes, forms the exactly-rounded 16-bit
 //               weights and writes them straight into the stage's TMEM A slot
 //               with tcgen05.st (no shared-memory round trip), then signals
-//               deq[s]
+//               deq[s]; several warps per quarter hide the dequant latency
 //   MMA       : warp 1, one thread -- four tcgen05.mma (K = 16 each) per
 //               k-block, A from TMEM, B (x) from shared memory by descriptor,
 //               D (128 x 256 fp32) accumulating in TMEM; tcgen05.commit frees
 //               the stage (empty[s]) and, after the last k-block, publishes
 //               the tile (acc_full)
-//   epilogue  : warps 8..11 -- tcgen05.ld of the accumulator, fp32 stores
+//   epilogue  : warps 4..7 -- tcgen05.ld of the accumulator, fp32 stores
 //               (each warp store is 32 consecutive weight rows of one batch
 //               row: 128 coalesced bytes), then acc_empty
 //   warp 2    : TMEM allocation / release (512 columns: accumulator 256 +
@@ -50,7 +51,11 @@ constexpr int kWBytes = kBN * kBK / 2;   // 4 KB packed tile per stage
 constexpr int kAccCols = kBX;            // fp32 accumulator columns
 constexpr int kACols = kBK / 2;          // TMEM columns of one A slot (two 16-bit values per column)
 constexpr int kTmemCols = 512;
-constexpr int kThreads = 384;            // 12 warps
+// Dequant warps per TMEM lane quarter: each fills 64 / kDqSplit columns of a
+// k-block, so one k-block is spread over 4 * kDqSplit warps.
+constexpr int kDqSplit = 1;
+constexpr int kDqWords = 8 / kDqSplit;   // packed words per dequant thread per k-block
+constexpr int kThreads = 256 + 128 * kDqSplit;  // warps 0-3 control, 4-7 epilogue, 8.. dequant
 constexpr size_t kSmemBytes = 1024 + (size_t)kStages * (kXBytes + kWBytes) + 256;
 
 static_assert(kAccCols + kStages * kACols <= kTmemCols, "TMEM budget");
@@ -80,7 +85,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&full[s], 1);   // producer's expect_tx arrival
-            mbar_init(&deq[s], 4);    // one arrival per dequant warp
+            mbar_init(&deq[s], 4 * kDqSplit);  // one arrival per dequant warp
             mbar_init(&empty[s], 1);  // tcgen05.commit
         }
         mbar_init(acc_full, 1);
@@ -150,9 +155,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_commit(mma_done);
             mbar_wait(mma_done, 0);
         }
-    } else if (warp >= 4 && warp < 8) {
+    } else if (warp >= 8) {
         // ------------------------------------------------------- dequant
-        const int q = warp - 4;         // TMEM lane quarter
+        const int d = warp - 8;
+        const int q = d & 3;            // TMEM lane quarter (= warp % 4)
+        const int part = d >> 2;        // which kDqWords words of the row's k-block
         const int r = q * 32 + lane;    // weight row within the tile
         int it = 0;
         bool ok = true;
@@ -162,23 +169,36 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int kb = 0; kb < kblocks; ++kb, ++it) {
                 const int s = it % kStages, rd = it / kStages;
                 const int c0 = kb * kBK;
+                // words 0-3 of a row's k-block are columns c0..c0+31 (scale
+                // s0), words 4-7 the next 32 (s1)
                 const float s0 = __ldg(srow + min(c0 / g, groups - 1));
-                const float s1 = __ldg(srow + min((c0 + 32) / g, groups - 1));
+                const float s1 = kDqSplit == 1 || part * kDqWords >= 4 ? __ldg(srow + min((c0 + 32) / g, groups - 1))
+                                                                      : s0;
                 // Warp-uniform outcome: tcgen05.st below is .sync.aligned.
                 ok = __all_sync(0xffffffffu, mbar_wait(&full[s], rd & 1));
                 if (!ok) break;
-                const uint4 w0 = *reinterpret_cast<const uint4 *>(wbuf + (size_t)s * kWBytes + r * 32);
-                const uint4 w1 = *reinterpret_cast<const uint4 *>(wbuf + (size_t)s * kWBytes + r * 32 + 16);
-                const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+                uint32_t words[kDqWords];
+                const uint8_t *src = wbuf + (size_t)s * kWBytes + r * 32 + part * kDqWords * 4;
+                if constexpr (kDqWords % 4 == 0) {
+#pragma unroll
+                    for (int v = 0; v < kDqWords; v += 4) {
+                        const uint4 wv = *reinterpret_cast<const uint4 *>(src + 4 * v);
+                        words[v] = wv.x, words[v + 1] = wv.y, words[v + 2] = wv.z, words[v + 3] = wv.w;
+                    }
+                } else {
+                    const uint2 wv = *reinterpret_cast<const uint2 *>(src);
+                    words[0] = wv.x, words[1] = wv.y;
+                }
                 const DqScale d0 = make_dq_scale(s0), d1 = make_dq_scale(s1);
-                uint32_t a[32];
+                uint32_t a[4 * kDqWords];
                 auto run = [&](auto fast_tag) {
                     constexpr bool FAST = decltype(fast_tag)::value;
 #pragma unroll
-                    for (int wd = 0; wd < 8; ++wd) {
+                    for (int wd = 0; wd < kDqWords; ++wd) {
+                        const DqScale &ds = part * kDqWords + wd < 4 ? d0 : d1;
                         uint32_t h0[2], h1[2];
-                        dq_half<XT, 0, FAST>(words[wd], wd < 4 ? d0 : d1, h0);
-                        dq_half<XT, 1, FAST>(words[wd], wd < 4 ? d0 : d1, h1);
+                        dq_half<XT, 0, FAST>(words[wd], ds, h0);
+                        dq_half<XT, 1, FAST>(words[wd], ds, h1);
                         a[4 * wd + 0] = h0[0];
                         a[4 * wd + 1] = h0[1];
                         a[4 * wd + 2] = h1[0];
@@ -189,16 +209,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                     run(std::true_type{});
                 else
                     run(std::false_type{});
-                tmem_st_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + kAccCols + s * kACols, a);
+                tmem_st_32x32b<4 * kDqWords>(
+                    tmem + ((uint32_t)(q * 32) << 16) + kAccCols + s * kACols + part * 4 * kDqWords, a);
                 tc_wait_st();
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&deq[s]);
             }
         }
-    } else if (warp >= 8) {
+    } else if (warp >= 4) {
         // ------------------------------------------------------ epilogue
-        const int q = warp - 8;
+        const int q = warp - 4;
         int ti = 0;
         bool ok = true;
         for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++ti) {
