@@ -6,8 +6,8 @@ x16 @ restored16.T with assert_close(rtol=atol=0.02), timed as the median of
 30 calls, the fastest reported).  Here every candidate is a hand-written
 sm_100a kernel and launch shape of oq_int4_linear -- the TMA-fed and
 register-ring GEMVs, the tcgen05 GEMM and the CUDA-core kernel -- checked the
-same way, timed the against the same reference, timed as back-to-back launches in a CUDA graph
-over rotated weight copies (the way a decode step runs them), and the winner
+same way against the same reference, timed as back-to-back launches in a CUDA
+graph over rotated weight copies (the way a decode step runs them), and the winner
 per (M bucket, N, K, g) is written to openquant_b200/tile_table.json, which
 int4_linear reads.
 """
@@ -40,11 +40,16 @@ SHAPES += [(m, k, n, 128, torch.bfloat16) for m in (512, 2048) for k, n in ((819
 
 
 def candidates(m):
-    """(name, kernel code, config) pairs worth trying at batch size m."""
-    out = []
+    """(name, kernel code, config) pairs worth trying at batch size m; the
+    library's own shape rule ("auto") is one of them, so a table entry is
+    never slower than leaving the shape out."""
+    out = [("auto", 0, 0)]
     if m <= 64:
         shapes = [*range(1, 11), 12, 13] if m <= 16 else range(1, 8)
-        out += [(f"gemv:{c}", nat.KERNELS["gemv"], c) for c in shapes]
+        # Above M = 8 the library's default is the exact weight rounding; a
+        # table entry changes the launch shape, never the rounding.
+        flag = nat.CONFIG_EXACT_ROUNDING if m > 8 else 0
+        out += [(f"gemv:{c}", nat.KERNELS["gemv"], c | flag) for c in shapes]
     out.append(("tcgen05", nat.KERNELS["tcgen05"], 0))
     if m <= 256:
         out.append(("simt", nat.KERNELS["simt"], 0))

@@ -121,12 +121,21 @@ def int4_linear(x, packed, scales, out_features, group_size, *, block_m=64, bloc
     if static_weights:
         split |= nat.CONFIG_STATIC_WEIGHTS
     code = nat.OQ_F16 if x.dtype == torch.float16 else nat.OQ_BF16
-    with torch.cuda.device(x.device):
+    from_table = kernel is None and not silu_gate and (sel, split & 15) != (0, 0)
+
+    def run(sel, split):
         if bias is None and out.dtype == torch.float32 and not silu_gate:
-            nat.check(nat.load().oq_int4_linear(nat.ptr(x), code, nat.ptr(packed), nat.ptr(scales), nat.ptr(out),
-                                                m, n, k, g, sel, split, nat.stream_of(x.device)))
-        else:
-            nat.check(nat.load().oq_int4_linear_ex(nat.ptr(x), code, nat.ptr(packed), nat.ptr(scales), nat.ptr(out),
-                                                   ycodes[out.dtype], nat.ptr(bias) if bias is not None else None,
-                                                   m, n, k, g, sel, split, nat.stream_of(x.device)))
+            return nat.load().oq_int4_linear(nat.ptr(x), code, nat.ptr(packed), nat.ptr(scales), nat.ptr(out),
+                                             m, n, k, g, sel, split, nat.stream_of(x.device))
+        return nat.load().oq_int4_linear_ex(nat.ptr(x), code, nat.ptr(packed), nat.ptr(scales), nat.ptr(out),
+                                            ycodes[out.dtype], nat.ptr(bias) if bias is not None else None,
+                                            m, n, k, g, sel, split, nat.stream_of(x.device))
+
+    with torch.cuda.device(x.device):
+        status = run(sel, split)
+        if status == nat.OQ_ERR_INVALID and from_table:
+            # A tuned launch shape is chosen per batch-size bucket; a smaller or
+            # larger M in the bucket can fall outside its shared-memory plan.
+            status = run(0, split & ~15)
+        nat.check(status)
     return out
