@@ -3,6 +3,7 @@
 
 #include <map>
 #include <mutex>
+#include <unordered_map>
 #include <vector>
 
 namespace oq {
@@ -83,27 +84,58 @@ void register_device_error_reader(DeviceErrorReader fn) {
     readers().push_back(fn);
 }
 
+namespace {
+// Encoded maps by their arguments: a decode step re-launches on the same
+// weights, and a map depends on nothing but these arguments, so a cached map
+// is the one the encoder would return.
+struct MapKey {
+    const void *base;
+    int dtype, esize, swizzle;
+    uint64_t inner, outer, pitch;
+    uint32_t box_inner, box_outer;
+    bool operator==(const MapKey &o) const {
+        return base == o.base && dtype == o.dtype && esize == o.esize && swizzle == o.swizzle && inner == o.inner &&
+               outer == o.outer && pitch == o.pitch && box_inner == o.box_inner && box_outer == o.box_outer;
+    }
+};
+struct MapKeyHash {
+    size_t operator()(const MapKey &k) const {
+        uint64_t h = reinterpret_cast<uintptr_t>(k.base) * 0x9E3779B97F4A7C15ull;
+        for (uint64_t v : {(uint64_t)k.dtype, (uint64_t)k.esize, (uint64_t)k.swizzle, k.inner, k.outer, k.pitch,
+                           (uint64_t)k.box_inner, (uint64_t)k.box_outer})
+            h = (h ^ v) * 0x100000001B3ull;
+        return (size_t)h;
+    }
+};
+constexpr size_t kMapCacheEntries = 1024;
+}  // namespace
+
 int make_tensor_map_2d(CUtensorMap *map, const void *base, CUtensorMapDataType dtype, int esize, uint64_t inner,
                        uint64_t outer, uint64_t pitch_bytes, uint32_t box_inner, uint32_t box_outer,
                        CUtensorMapSwizzle swizzle) {
     static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
     static std::mutex mu;
-    {
-        std::lock_guard<std::mutex> lock(mu);
-        if (encode == nullptr) {
-            cudaDriverEntryPointQueryResult q;
-            void *fn = nullptr;
-            cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
-            if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || fn == nullptr) {
-                set_error("cuTensorMapEncodeTiled unavailable (driver too old?)");
-                return OQ_ERR_UNSUPPORTED;
-            }
-            encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-        }
-    }
+    static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache;
     if (!aligned(base, 16) || pitch_bytes % 16 != 0 || (uint64_t)box_inner * esize % 16 != 0) {
         set_error("tensor map: base, pitch and box row must be 16-byte multiples");
         return OQ_ERR_INVALID;
+    }
+    const MapKey key{base, (int)dtype, esize, (int)swizzle, inner, outer, pitch_bytes, box_inner, box_outer};
+    std::lock_guard<std::mutex> lock(mu);
+    auto hit = cache.find(key);
+    if (hit != cache.end()) {
+        *map = hit->second;
+        return OQ_OK;
+    }
+    if (encode == nullptr) {
+        cudaDriverEntryPointQueryResult q;
+        void *fn = nullptr;
+        cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+        if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || fn == nullptr) {
+            set_error("cuTensorMapEncodeTiled unavailable (driver too old?)");
+            return OQ_ERR_UNSUPPORTED;
+        }
+        encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
     }
     cuuint64_t dims[2] = {inner, outer};
     cuuint64_t strides[1] = {pitch_bytes};
@@ -115,6 +147,8 @@ int make_tensor_map_2d(CUtensorMap *map, const void *base, CUtensorMapDataType d
         set_error("cuTensorMapEncodeTiled failed (code %d)", (int)r);
         return OQ_ERR_CUDA;
     }
+    if (cache.size() >= kMapCacheEntries) cache.clear();
+    cache.emplace(key, *map);
     return OQ_OK;
 }
 

@@ -16,6 +16,17 @@ from . import tile_table
 
 __all__ = ["int4_linear"]
 
+_YCODES = {torch.float32: nat.OQ_F32, torch.float16: nat.OQ_F16, torch.bfloat16: nat.OQ_BF16}
+# The current stream's handle of a device without building a Stream object
+# (a decode step calls int4_linear once per layer: host overhead counts).
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
+def _stream_handle(dev):
+    if _raw_stream is not None:
+        return _raw_stream(dev)
+    return torch.cuda.current_stream(dev).cuda_stream
+
 
 def int4_linear(x, packed, scales, out_features, group_size, *, block_m=64, block_n=64, block_k=64, num_warps=4,
                 kernel=None, out=None, exact_rounding=False, static_weights=False, bias=None, out_dtype=None,
@@ -85,24 +96,25 @@ def int4_linear(x, packed, scales, out_features, group_size, *, block_m=64, bloc
         raise ValueError("silu_gate takes no bias and needs M <= 16")
     if not packed.is_contiguous() or not scales.is_contiguous():
         raise ValueError("Weights and scales must be contiguous")
-    if packed.device != x.device or scales.device != x.device:
+    dev = x.get_device()
+    if packed.get_device() != dev or scales.get_device() != dev:
         raise ValueError("All tensors must use the same GPU")
     for v in (block_m, block_n, block_k, num_warps):
         if int(v) < 1:
             raise ValueError("Tile arguments must be positive")
 
-    ycodes = {torch.float32: nat.OQ_F32, torch.float16: nat.OQ_F16, torch.bfloat16: nat.OQ_BF16}
+    ycodes = _YCODES
     if out is None:
         odt = torch.float32 if out_dtype is None else out_dtype
         if odt not in ycodes:
             raise ValueError("out_dtype must be torch.float32, torch.float16 or torch.bfloat16")
         out = torch.empty((m, n), device=x.device, dtype=odt)
-    elif (out.shape != (m, n) or out.dtype not in ycodes or out.device != x.device or not out.is_contiguous()
+    elif (out.shape != (m, n) or out.dtype not in ycodes or out.get_device() != dev or not out.is_contiguous()
           or (out_dtype is not None and out.dtype != out_dtype)):
         raise ValueError("out must be a contiguous float32, float16 or bfloat16 (M, N) tensor on x's device")
     if bias is not None:
         if (not isinstance(bias, torch.Tensor) or bias.dtype != torch.float32 or bias.numel() != n
-                or bias.device != x.device or not bias.is_contiguous()):
+                or bias.get_device() != dev or not bias.is_contiguous()):
             raise ValueError("bias must be a contiguous float32 tensor of N elements on x's device")
 
     nat.require_device()
@@ -123,19 +135,29 @@ def int4_linear(x, packed, scales, out_features, group_size, *, block_m=64, bloc
     code = nat.OQ_F16 if x.dtype == torch.float16 else nat.OQ_BF16
     from_table = kernel is None and not silu_gate and (sel, split & 15) != (0, 0)
 
-    def run(sel, split):
-        if bias is None and out.dtype == torch.float32 and not silu_gate:
-            return nat.load().oq_int4_linear(nat.ptr(x), code, nat.ptr(packed), nat.ptr(scales), nat.ptr(out),
-                                             m, n, k, g, sel, split, nat.stream_of(x.device))
-        return nat.load().oq_int4_linear_ex(nat.ptr(x), code, nat.ptr(packed), nat.ptr(scales), nat.ptr(out),
-                                            ycodes[out.dtype], nat.ptr(bias) if bias is not None else None,
-                                            m, n, k, g, sel, split, nat.stream_of(x.device))
+    lib = nat.load()
+    ptrs = (x.data_ptr(), packed.data_ptr(), scales.data_ptr(), out.data_ptr())
+    plain = bias is None and out.dtype == torch.float32 and not silu_gate
 
-    with torch.cuda.device(x.device):
+    def run(sel, split):
+        stream = _stream_handle(dev)
+        if plain:
+            return lib.oq_int4_linear(ptrs[0], code, ptrs[1], ptrs[2], ptrs[3], m, n, k, g, sel, split, stream)
+        return lib.oq_int4_linear_ex(ptrs[0], code, ptrs[1], ptrs[2], ptrs[3], ycodes[out.dtype],
+                                     bias.data_ptr() if bias is not None else None, m, n, k, g, sel, split, stream)
+
+    def launch():
         status = run(sel, split)
         if status == nat.OQ_ERR_INVALID and from_table:
             # A tuned launch shape is chosen per batch-size bucket; a smaller or
             # larger M in the bucket can fall outside its shared-memory plan.
             status = run(0, split & ~15)
         nat.check(status)
+
+    # The library works on the current device: switch only when x lives elsewhere.
+    if torch.cuda.current_device() == dev:
+        launch()
+    else:
+        with torch.cuda.device(dev):
+            launch()
     return out
