@@ -254,6 +254,216 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+// ---------------------------------------------------------- wide tiles --
+//
+// For M >= 1024: the same roles, but each dequantized A slot feeds two MMAs,
+// one per half of a batch tile of 2 * NB rows (NB <= 224, a multiple of 16),
+// into two accumulators -- half the weight dequantizations per flop of the
+// 256-row tiles above, which the exact rounding makes the costly part.
+// TMEM: accumulators in columns [0, 2 NB), two A slots of 32 columns at 448.
+// Shared memory: 3 stages of (2 NB x 128 B of x, loaded as two NB-row TMA
+// boxes, + the 4 KB packed tile).  The A-slot ring (2) is decoupled from the
+// stage ring (3): deq[a] publishes a written slot, a_empty[a] (tcgen05.commit)
+// frees it for the dequant warps.
+constexpr int kWideStages = 3;
+constexpr int kWideMaxNB = 224;
+constexpr int kWideXBytes = 2 * kWideMaxNB * kBK * 2;  // 56 KB x tile per stage
+constexpr int kWideACol = 448;                           // first A-slot column
+constexpr size_t kWideSmemBytes = 1024 + (size_t)kWideStages * (kWideXBytes + kWBytes) + 256;
+
+static_assert(kWideACol + 2 * kACols <= kTmemCols, "wide TMEM budget");
+
+template <typename XT>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_int4_tcgen05_wide_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
+                                  const float *__restrict__ scales, OutSpec y, int m, int n, int kp, int g, int nb) {
+    static_assert(kDqSplit == 1, "the wide kernel keeps one dequant warp per TMEM lane quarter");
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+    uint8_t *xbuf = smem;                                        // [S][2 nb rows][128 B], swizzled
+    uint8_t *wbuf = xbuf + (size_t)kWideStages * kWideXBytes;    // [S][128 rows][32 B]
+    uint64_t *full = reinterpret_cast<uint64_t *>(wbuf + (size_t)kWideStages * kWBytes);
+    uint64_t *empty = full + kWideStages;
+    uint64_t *deq = empty + kWideStages;  // [2] A slots
+    uint64_t *a_empty = deq + 2;          // [2]
+    uint64_t *acc_full = a_empty + 2;
+    uint64_t *acc_empty = acc_full + 1;
+    uint64_t *mma_done = acc_empty + 1;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mma_done + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int bx = 2 * nb;  // batch rows per tile
+    const int tiles_n = (n + kBN - 1) / kBN, tiles_m = (m + bx - 1) / bx;
+    const int tiles = tiles_n * tiles_m;
+    const int kblocks = (kp + kBK - 1) / kBK;
+    const int groups = kp / g;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kWideStages; ++s) {
+            mbar_init(&full[s], 1);   // producer's expect_tx arrival
+            mbar_init(&empty[s], 1);  // tcgen05.commit
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&deq[a], 4);      // one arrival per dequant warp
+            mbar_init(&a_empty[a], 1);  // tcgen05.commit
+        }
+        mbar_init(acc_full, 1);
+        mbar_init(acc_empty, 4);
+        mbar_init(mma_done, 1);
+        fence_barrier_init();
+    }
+    if (warp == 2) {
+        tmem_alloc(tmem_slot, kTmemCols);
+        tmem_relinquish();
+        tc_fence_before();
+    }
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;");
+
+    if (warp == 0) {
+        // ------------------------------------------------------ producer
+        if (lane == 0) {
+            tma_prefetch_desc(&xmap);
+            tma_prefetch_desc(&wmap);
+            int it = 0;
+            bool ok = true;
+            const uint32_t tx = (uint32_t)(bx * kBK * 2 + kWBytes);
+            for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+                const int n0 = (tile / tiles_m) * kBN, m0 = (tile % tiles_m) * bx;
+                for (int kb = 0; kb < kblocks; ++kb, ++it) {
+                    const int s = it % kWideStages, r = it / kWideStages;
+                    if (r > 0 && !(ok = mbar_wait(&empty[s], (r - 1) & 1))) break;
+                    uint8_t *xs = xbuf + (size_t)s * kWideXBytes;
+                    mbar_arrive_expect_tx(&full[s], tx);
+                    tma_load_2d(xs, &xmap, &full[s], kb * kBK, m0);
+                    tma_load_2d(xs + nb * 128, &xmap, &full[s], kb * kBK, m0 + nb);
+                    tma_load_2d(wbuf + (size_t)s * kWBytes, &wmap, &full[s], kb * (kBK / 2), n0);
+                }
+            }
+            // Drain: every issued stage's copies land before the CTA exits.
+            for (int j = (it > kWideStages ? it - kWideStages : 0); j < it; ++j)
+                mbar_wait(&full[j % kWideStages], (j / kWideStages) & 1);
+        }
+    } else if (warp == 1) {
+        // ----------------------------------------------------------- MMA
+        if (lane == 0) {
+            const uint32_t idesc = umma_idesc_f16(kBN, nb, std::is_same<XT, __nv_bfloat16>::value);
+            int it = 0, ti = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++ti) {
+                if (ti > 0 && !(ok = mbar_wait(acc_empty, (ti - 1) & 1))) break;
+                tc_fence_after();
+                for (int kb = 0; kb < kblocks; ++kb, ++it) {
+                    const int s = it % kWideStages, a = it & 1;
+                    if (!(ok = mbar_wait(&full[s], (it / kWideStages) & 1))) break;
+                    if (!(ok = mbar_wait(&deq[a], (it >> 1) & 1))) break;
+                    tc_fence_after();
+                    const uint32_t xaddr = smem_u32(xbuf + (size_t)s * kWideXBytes);
+                    const uint64_t b0 = umma_desc_sw128(xaddr), b1 = umma_desc_sw128(xaddr + nb * 128);
+                    const uint32_t a_tmem = tmem + kWideACol + a * kACols;
+#pragma unroll
+                    for (int kk = 0; kk < kBK / 16; ++kk) {
+                        const uint32_t acc = (kb | kk) != 0 ? 1u : 0u;
+                        tc_mma_ts(tmem, a_tmem + kk * 8, b0 + (uint64_t)(kk * 32 / 16), idesc, acc);
+                        tc_mma_ts(tmem + nb, a_tmem + kk * 8, b1 + (uint64_t)(kk * 32 / 16), idesc, acc);
+                    }
+                    tc_commit(&empty[s]);
+                    tc_commit(&a_empty[a]);
+                }
+                if (ok) tc_commit(acc_full);
+            }
+            // Every MMA this thread issued has completed once mma_done fires.
+            tc_commit(mma_done);
+            mbar_wait(mma_done, 0);
+        }
+    } else if (warp >= 8) {
+        // ------------------------------------------------------- dequant
+        const int q = warp - 8;         // TMEM lane quarter
+        const int r = q * 32 + lane;    // weight row within the tile
+        int it = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+            const int n0 = (tile / tiles_m) * kBN;
+            const float *srow = scales + (size_t)min(n0 + r, n - 1) * groups;
+            for (int kb = 0; kb < kblocks; ++kb, ++it) {
+                const int s = it % kWideStages, a = it & 1;
+                const int c0 = kb * kBK;
+                const float s0 = __ldg(srow + min(c0 / g, groups - 1));
+                const float s1 = __ldg(srow + min((c0 + 32) / g, groups - 1));
+                // Warp-uniform outcomes: tcgen05.st below is .sync.aligned.
+                ok = __all_sync(0xffffffffu, mbar_wait(&full[s], (it / kWideStages) & 1));
+                if (ok && it >= 2) ok = __all_sync(0xffffffffu, mbar_wait(&a_empty[a], ((it >> 1) - 1) & 1));
+                if (!ok) break;
+                const uint4 w0 = *reinterpret_cast<const uint4 *>(wbuf + (size_t)s * kWBytes + r * 32);
+                const uint4 w1 = *reinterpret_cast<const uint4 *>(wbuf + (size_t)s * kWBytes + r * 32 + 16);
+                const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+                const DqScale d0 = make_dq_scale(s0), d1 = make_dq_scale(s1);
+                uint32_t av[32];
+                auto run = [&](auto fast_tag) {
+                    constexpr bool FAST = decltype(fast_tag)::value;
+#pragma unroll
+                    for (int wd = 0; wd < 8; ++wd) {
+                        uint32_t h0[2], h1[2];
+                        dq_half<XT, 0, FAST>(words[wd], wd < 4 ? d0 : d1, h0);
+                        dq_half<XT, 1, FAST>(words[wd], wd < 4 ? d0 : d1, h1);
+                        av[4 * wd + 0] = h0[0];
+                        av[4 * wd + 1] = h0[1];
+                        av[4 * wd + 2] = h1[0];
+                        av[4 * wd + 3] = h1[1];
+                    }
+                };
+                if (__all_sync(0xffffffffu, d0.fast && d1.fast))
+                    run(std::true_type{});
+                else
+                    run(std::false_type{});
+                tmem_st_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + kWideACol + a * kACols, av);
+                tc_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&deq[a]);
+            }
+        }
+    } else if (warp >= 4) {
+        // ------------------------------------------------------ epilogue
+        const int q = warp - 4;
+        int ti = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++ti) {
+            const int n0 = (tile / tiles_m) * kBN, m0 = (tile % tiles_m) * bx;
+            ok = __all_sync(0xffffffffu, mbar_wait(acc_full, ti & 1));  // tcgen05.ld is .sync.aligned
+            if (!ok) break;
+            tc_fence_after();
+            const int row = n0 + q * 32 + lane;
+#pragma unroll 1
+            for (int c = 0; c < bx / 32; ++c) {
+                uint32_t v[32];
+                tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + c * 32, v);
+                tc_wait_ld();
+                if (row < n) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const int mb = m0 + c * 32 + j;
+                        if (mb < m) y.store((size_t)mb * n + row, row, __uint_as_float(v[j]));
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acc_empty);
+        }
+    }
+
+    __syncthreads();
+    if (warp == 2) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
 int allow_smem(const void *kern, size_t bytes) {
     static std::mutex mu;
     static std::set<std::pair<const void *, int>> done;
@@ -266,9 +476,69 @@ int allow_smem(const void *kern, size_t bytes) {
     return OQ_OK;
 }
 
+// Batch rows from which the wide-tile kernel is considered: below it the
+// 256-row tiles waste less on the ragged last tile than the wide ones save.
+constexpr int64_t kWideMinM = 1024;
+
+// NB of the wide tiles for M: the fewest tiles of at most 2 x 224 rows, then
+// the smallest NB (a multiple of 16) whose tiles cover M.
+inline int wide_nb(int64_t m) {
+    const int64_t tiles_m = cdiv(m, 2 * kWideMaxNB);
+    return (int)std::min<int64_t>(kWideMaxNB, cdiv(cdiv(cdiv(m, tiles_m), 2), 16) * 16);
+}
+
+// Wide or 256-row tiles: a wave model of the persistent grid -- rounds of
+// tiles over the SMs, each tile costing its batch rows plus the dequant of
+// its weight tile (about 128 rows' worth, measured) -- which picks the
+// faster kind on every prefill shape measured (the wide tiles lose where
+// they leave too few tiles for the last round, e.g. N = 8192 at M = 1024).
+inline bool use_wide_tiles(int64_t m, int64_t n) {
+    if (m < kWideMinM) return false;
+    constexpr int64_t kDequantRows = 128;
+    const int64_t sms = sm_count(), tiles_n = cdiv(n, kBN), nb = wide_nb(m);
+    const int64_t narrow = cdiv(tiles_n * cdiv(m, kBX), sms) * (kBX + kDequantRows);
+    const int64_t wide = cdiv(tiles_n * cdiv(m, 2 * nb), sms) * (2 * nb + kDequantRows);
+    return wide < narrow;
+}
+
+template <typename XT>
+int launch_wide(const XT *x, CUtensorMapDataType xtype, const uint8_t *packed, const float *scales, OutSpec y,
+                int64_t m, int64_t n, int64_t k, int g, cudaStream_t st) {
+    const int64_t kp = cdiv(k, g) * g;
+    const int nb = wide_nb(m);
+    CUtensorMap xmap, wmap;
+    int rc = make_tensor_map_2d(&xmap, x, xtype, 2, (uint64_t)k, (uint64_t)m, (uint64_t)(k * 2), kBK, (uint32_t)nb,
+                                CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != OQ_OK) return rc;
+    rc = make_tensor_map_2d(&wmap, packed, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)(kp / 2), (uint64_t)n,
+                            (uint64_t)(kp / 2), kBK / 2, kBN, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc != OQ_OK) return rc;
+    auto kern = gemm_int4_tcgen05_wide_kernel<XT>;
+    rc = allow_smem(reinterpret_cast<const void *>(kern), kWideSmemBytes);
+    if (rc != OQ_OK) return rc;
+    const int64_t tiles = cdiv(n, kBN) * cdiv(m, 2 * (int64_t)nb);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)std::min<int64_t>(tiles, sm_count()));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kWideSmemBytes;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t err = cudaLaunchKernelEx(&cfg, kern, xmap, wmap, scales, y, (int)m, (int)n, (int)kp, g, nb);
+    if (err != cudaSuccess) {
+        set_error("int4_linear (tcgen05 GEMM, wide tiles): launch failed: %s", cudaGetErrorString(err));
+        return OQ_ERR_CUDA;
+    }
+    return OQ_OK;
+}
+
 template <typename XT>
 int launch(const XT *x, CUtensorMapDataType xtype, const uint8_t *packed, const float *scales, OutSpec y, int64_t m,
            int64_t n, int64_t k, int g, cudaStream_t st) {
+    if (use_wide_tiles(m, n)) return launch_wide(x, xtype, packed, scales, y, m, n, k, g, st);
     const int64_t kp = cdiv(k, g) * g;
     CUtensorMap xmap, wmap;
     int rc = make_tensor_map_2d(&xmap, x, xtype, 2, (uint64_t)k, (uint64_t)m, (uint64_t)(k * 2), kBK, kBX,

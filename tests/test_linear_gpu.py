@@ -228,13 +228,17 @@ def test_deterministic_repeat():
 PREFILL_SHAPES = [
     (64, 128, 64, 32), (100, 200, 136, 64), (256, 256, 1024, 128), (300, 129, 520, 32), (17, 1000, 4096, 128),
     (512, 1024, 2048, 128), (513, 384, 8192, 128), (1024, 128, 200, 64),
+    # large N at M >= 1024: the wide-tile kernel (two accumulators of NB rows),
+    # ragged in M and N
+    (1500, 20000, 256, 32), (2050, 18000, 512, 128), (4097, 9000, 256, 64),
 ]
 
 
 @pytest.mark.parametrize("shape", PREFILL_SHAPES)
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 def test_prefill_tcgen05_vs_oracle(shape, dtype):
-    """The tcgen05/TMEM GEMM against the oracle (ragged M, N, K; g 32..128)."""
+    """The tcgen05/TMEM GEMM against the oracle (ragged M, N, K; g 32..128;
+    256-row tiles, and the wide tiles the launcher picks for large M and N)."""
     from openquant.triton_int4 import int4_linear
 
     m, n, k, g = shape
