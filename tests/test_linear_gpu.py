@@ -331,7 +331,8 @@ def test_fp16_scale_after_vs_exact_rounding(shape):
 
 @pytest.mark.parametrize("kernel", ["gemv", "simt", "tcgen05", None])
 @pytest.mark.parametrize("out_dtype", [torch.float32, torch.float16, torch.bfloat16])
-@pytest.mark.parametrize("shape", [(1, 4096, 4096, 128), (5, 300, 1024, 64), (300, 640, 1024, 128)])
+@pytest.mark.parametrize("shape", [(1, 4096, 4096, 128), (5, 300, 1024, 64), (300, 640, 1024, 128),
+                                   (1100, 9000, 256, 128)])  # the last: wide GEMM tiles
 def test_fused_bias_and_output_dtype(shape, out_dtype, kernel):
     """The fused epilogue adds the bias in fp32 and rounds once, exactly as
     (fp32 result + bias).to(dtype) does."""
@@ -419,3 +420,23 @@ def test_silu_gate_fusion_matches_two_products(shape, dtype):
     assert torch.equal(yb, fused.to(torch.bfloat16))
     with pytest.raises(ValueError):
         int4_linear(x, q.data, q.scales, n, g, silu_gate=True, bias=torch.zeros(n, device="cuda"))
+
+
+def test_tile_table_entry_outside_its_plan_falls_back(monkeypatch):
+    """A tuned table entry holds for a whole batch-size bucket; when its
+    launch shape rejects the call (here the tile GEMV, which needs KP <=
+    4096, given K = 8192) int4_linear runs the library's automatic choice
+    instead of failing, with the same result."""
+    from openquant.triton_int4 import int4_linear
+    from openquant_b200 import _native as nat
+    from openquant_b200 import tile_table
+
+    m, n, k, g = 4, 256, 8192, 128
+    x, q, xt = make_case(m, n, k, g, torch.float16, seed=11, w_sigma=0.02)
+    p, s = torch.from_numpy(q.data).cuda(), torch.from_numpy(q.scales).cuda()
+    ref = int4_linear(xt, p, s, n, g)
+    monkeypatch.setattr(tile_table, "lookup", lambda *a: (nat.KERNELS["gemv"], 12))
+    y = int4_linear(xt, p, s, n, g)
+    assert torch.equal(y, ref)
+    check_against_oracle(y, x, q, g, torch.float16)
+
