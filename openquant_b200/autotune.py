@@ -46,9 +46,9 @@ def candidates(m):
     out = [("auto", 0, 0)]
     if m <= 64:
         shapes = [*range(1, 11), 12, 13] if m <= 16 else range(1, 8)
-        # Above M = 8 the library's default is the exact weight rounding; a
+        # Above M = 16 the library's default is the exact weight rounding; a
         # table entry changes the launch shape, never the rounding.
-        flag = nat.CONFIG_EXACT_ROUNDING if m > 8 else 0
+        flag = nat.CONFIG_EXACT_ROUNDING if m > 16 else 0
         out += [(f"gemv:{c}", nat.KERNELS["gemv"], c | flag) for c in shapes]
     out.append(("tcgen05", nat.KERNELS["tcgen05"], 0))
     if m <= 256:

@@ -27,20 +27,22 @@ template <typename XT, int NT, bool XS, bool FAST>
 __device__ __forceinline__ void gemv_chunk(int c, const uint32_t (&qa)[4], const uint32_t (&qb)[4],
                                            const DqScale &dsa, const DqScale &dsb, const uint32_t (&xaddr)[NT],
                                            const bool (&xon)[NT], const XT *const (&xg)[NT], uint4 (&xb)[NT],
-                                           float (&acc)[2][NT][4]) {
+                                           float (&acc)[2][NT][4], int xo = 8) {
+    // xo: x offset per word step -- 8 for lanes holding 32 consecutive
+    // columns, 32 for the ldsm_x4 layout (see gemv_chunk_sa's TX)
 #pragma unroll
     for (int wd = 0; wd < 4; ++wd) {
 #pragma unroll
         for (int j = 0; j < NT; ++j) {
             if (XS) {
-                const uint32_t addr = xaddr[j] + (uint32_t)(128 * c + 8 * wd) * 2u;
+                const uint32_t addr = xaddr[j] + (uint32_t)(128 * c + xo * wd) * 2u;
                 asm volatile(
                     "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
                     " @p ld.shared.v4.u32 {%0, %1, %2, %3}, [%5];\n}\n"
                     : "+r"(xb[j].x), "+r"(xb[j].y), "+r"(xb[j].z), "+r"(xb[j].w)
                     : "r"((int)xon[j]), "r"(addr));
             } else if (xon[j]) {
-                xb[j] = __ldg(reinterpret_cast<const uint4 *>(xg[j] + 128 * c + 8 * wd));
+                xb[j] = __ldg(reinterpret_cast<const uint4 *>(xg[j] + 128 * c + xo * wd));
             }
         }
         // k16 step 0: nibbles 0-3 (pairs 0, 1); step 1: nibbles 4-7.
@@ -63,6 +65,15 @@ __device__ __forceinline__ void gemv_chunk(int c, const uint32_t (&qa)[4], const
     }
 }
 
+// Padding (fp16 elements) after each staged x row: rows then start 16 banks
+// apart, so the 8 lanes of a quarter-warp (rows g, g + 1 x 4 column
+// offsets 8 t) read distinct banks.
+constexpr int kXPad = 32;
+// The TMA-fed GEMVs use that layout when a chunk lies in one scale group (g
+// >= 128); otherwise, and in the register-ring kernel, lanes read x at 32 t +
+// 8 wd, where 8 elements of padding spread the rows best.
+inline int gemv_xpad(int g) { return g >= 128 ? kXPad : 8; }
+
 // Bytes of the GEMV's double-buffered cross-warp reduction buffer.
 __host__ __device__ constexpr size_t gemv_red_bytes(int warps, int nt) { return 2u * warps * nt * 4 * 32 * 4; }
 
@@ -80,6 +91,19 @@ __host__ __device__ constexpr size_t gemv_red_bytes(int warps, int nt) { return 
 // Products of fp16 q and x are exact (x / 16 too, unless it falls below the
 // fp16 normal range, |x| < 2^-10) and the tensor core sums them in fp32;
 // y += s * sum per chunk.
+// Four 8x8 b16 matrices from shared memory (ldmatrix): lane L gives the
+// address of row L % 8 of matrix L / 8 and receives, from each matrix j,
+// the 32-bit word L % 4 of row L / 4 in r[j].  On the 128-byte-swizzled
+// weight stages the 8 rows of one logical 16-byte unit lie in 8 distinct
+// bank groups, so the load is free of bank conflicts (a per-lane 16-byte
+// load of rows g, g+1 x 4 units is not: both rows' units share banks).
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr)
+                 : "memory");
+}
+
 __device__ __forceinline__ uint32_t lop3_and_xor(uint32_t a, uint32_t b, uint32_t c) {
     uint32_t d;
     asm("lop3.b32 %0, %1, %2, %3, 0x6A;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
@@ -149,7 +173,10 @@ __device__ __forceinline__ void gemv_stage_x(const XT *__restrict__ x, XT *xs, f
 // stay exact; the fp32 sums grow to ~1e3 |x|, so the result carries ~1e-3
 // absolute error per chunk (~1e-5 relative in y), below the reference's own
 // fp16 weight rounding.
-template <int NT, bool XS, bool FOLD = false>
+// TX (weights loaded with ldsm_x4): a lane's word wd holds chunk columns
+// 32 wd + 8 t .. + 7 instead of 32 t + 8 wd .. + 7, and x is read to match
+// (xaddr / xg then point at column 8 t).
+template <int NT, bool XS, bool FOLD = false, bool TX = false>
 __device__ __forceinline__ void gemv_chunk_sa(int c, const uint32_t (&qa)[4], const uint32_t (&qb)[4], float sa,
                                               float sb, const uint32_t (&xaddr)[NT], const bool (&xon)[NT],
                                               const __half *const (&xg)[NT], uint4 (&xb)[NT],
@@ -167,7 +194,7 @@ __device__ __forceinline__ void gemv_chunk_sa(int c, const uint32_t (&qa)[4], co
 #pragma unroll
         for (int j = 0; j < NT; ++j) {
             if (XS) {
-                const uint32_t addr = xaddr[j] + (uint32_t)(128 * c + 8 * wd) * 2u;
+                const uint32_t addr = xaddr[j] + (uint32_t)(128 * c + (TX ? 32 : 8) * wd) * 2u;
                 asm volatile(
                     "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
                     " @p ld.shared.v4.u32 {%0, %1, %2, %3}, [%5];\n}\n"
@@ -175,7 +202,7 @@ __device__ __forceinline__ void gemv_chunk_sa(int c, const uint32_t (&qa)[4], co
                     : "r"((int)xon[j]), "r"(addr));
             } else if (xon[j]) {
                 // natural order x0..x7 -> (x0,x4) (x2,x6) (x1,x5) (x3,x7)
-                xb[j] = sa_perm_x(__ldg(reinterpret_cast<const uint4 *>(xg[j] + 128 * c + 8 * wd)));
+                xb[j] = sa_perm_x(__ldg(reinterpret_cast<const uint4 *>(xg[j] + 128 * c + (TX ? 32 : 8) * wd)));
             }
         }
         const uint32_t wa = qa[wd], wb = qb[wd];
@@ -493,6 +520,9 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW <= 8 ? 2 : 1)
         gemv_stage_x<XT, SA, FOLD>(x, xs, corr, m, k, kp, xstride, CW * 32);
         asm volatile("bar.sync 1, %0;" ::"r"(CW * 32) : "memory");
     }
+    // ldsm_x4 weight loads and the matching x reads whenever a chunk lies in
+    // one scale group (always for scale-after): free of bank conflicts
+    const bool tx = SA || gshift >= 7;
     uint32_t xaddr[NT];
     bool xon[NT];
     const XT *xg[NT];
@@ -501,8 +531,8 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW <= 8 ? 2 : 1)
         const int mb = 8 * j + gi;
         xon[j] = mb < m;
         const int mr = xon[j] ? mb : 0;
-        xaddr[j] = smem_u32(xs) + (uint32_t)(mr * xstride + 32 * t) * 2u;
-        xg[j] = x + (size_t)mr * k + 32 * t;
+        xaddr[j] = smem_u32(xs) + (uint32_t)(mr * xstride + (tx ? 8 : 32) * t) * 2u;  // tx: ldsm_x4 layout
+        xg[j] = x + (size_t)mr * k + (tx ? 8 : 32) * t;
     }
     uint4 xb[NT];
 #pragma unroll
@@ -532,7 +562,8 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW <= 8 ? 2 : 1)
                 sreg[q][1] = __ldg(scales + (size_t)rb * groups + col);
             }
         }
-        if (ok) ok = mbar_wait(&full[slot], round & 1);
+        // warp-uniform: ldmatrix and mma.sync below are warp-collective
+        if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&full[slot], round & 1));
         if (ok) {
             const uint8_t *wst = wbuf + (size_t)slot * L::kStageBytes;
             const float *sst = reinterpret_cast<const float *>(reinterpret_cast<const uint8_t *>(sbuf) + (size_t)slot * sbytes);
@@ -541,25 +572,34 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW <= 8 ? 2 : 1)
                 const int c = st * CW * CPW + cs;        // chunk within the row
                 // Chunk cs = 64 bytes of each row: box cs/2, chunk
                 // ((cs%2)*4 + t) of the 128-byte row, swizzled by row % 8.
-                const uint32_t piece = (uint32_t)(cs >> 1) * 2048u + (uint32_t)gi * 128u +
-                                       (uint32_t)(((((cs & 1) << 2) + t) ^ (gi & 7)) << 4);
-                const uint4 wa = *reinterpret_cast<const uint4 *>(wst + piece);
-                const uint4 wb = *reinterpret_cast<const uint4 *>(wst + piece + 8 * 128);
+                uint32_t qa[4], qb[4];
+                if (tx) {  // warp-uniform
+                    const int lr = lane & 7, lj = lane >> 3;  // ldmatrix row / matrix of this lane
+                    const uint32_t a = smem_u32(wst) + (uint32_t)(cs >> 1) * 2048u + (uint32_t)lr * 128u +
+                                       (uint32_t)(((((cs & 1) << 2) + lj) ^ lr) << 4);
+                    ldsm_x4(a, qa);
+                    ldsm_x4(a + 8u * 128u, qb);
+                } else {
+                    const uint32_t piece = (uint32_t)(cs >> 1) * 2048u + (uint32_t)gi * 128u +
+                                           (uint32_t)(((((cs & 1) << 2) + t) ^ (gi & 7)) << 4);
+                    const uint4 wa = *reinterpret_cast<const uint4 *>(wst + piece);
+                    const uint4 wb = *reinterpret_cast<const uint4 *>(wst + piece + 8 * 128);
+                    qa[0] = wa.x, qa[1] = wa.y, qa[2] = wa.z, qa[3] = wa.w;
+                    qb[0] = wb.x, qb[1] = wb.y, qb[2] = wb.z, qb[3] = wb.w;
+                }
                 const int scol = (cs * 128 + 32 * t) >> gshift;
                 const float sa = STMA ? sst[gi * spr + scol] : sreg[q][0];
                 const float sb = STMA ? sst[(gi + 8) * spr + scol] : sreg[q][1];
                 const bool in = 128 * c + 32 * t < kp;
-                const uint32_t qa[4] = {wa.x, wa.y, wa.z, wa.w};
-                const uint32_t qb[4] = {wb.x, wb.y, wb.z, wb.w};
                 if constexpr (SA) {
-                    gemv_chunk_sa<NT, XS, FOLD>(c, qa, qb, in ? sa : 0.0f, in ? sb : 0.0f, xaddr, xon, xg, xb, acc,
+                    gemv_chunk_sa<NT, XS, FOLD, true>(c, qa, qb, in ? sa : 0.0f, in ? sb : 0.0f, xaddr, xon, xg, xb, acc,
                                                 corr + c * 16 + 2 * t);
                 } else {
                     const DqScale dsa = make_dq_scale(in ? sa : 0.0f), dsb = make_dq_scale(in ? sb : 0.0f);
                     if (__all_sync(0xffffffffu, dsa.fast && dsb.fast))
-                        gemv_chunk<XT, NT, XS, true>(c, qa, qb, dsa, dsb, xaddr, xon, xg, xb, acc);
+                        gemv_chunk<XT, NT, XS, true>(c, qa, qb, dsa, dsb, xaddr, xon, xg, xb, acc, tx ? 32 : 8);
                     else
-                        gemv_chunk<XT, NT, XS, false>(c, qa, qb, dsa, dsb, xaddr, xon, xg, xb, acc);
+                        gemv_chunk<XT, NT, XS, false>(c, qa, qb, dsa, dsb, xaddr, xon, xg, xb, acc, tx ? 32 : 8);
                 }
             };
             if (st * CW * CPW + (CPW - 1) * CW + warp < nchunks) {
@@ -667,6 +707,9 @@ __global__ void __launch_bounds__(256, 4)
     asm volatile("griddepcontrol.wait;" ::: "memory");
     if (XS) gemv_stage_x<XT, SA, FOLD>(x, xs, corr, m, k, kp, xstride, CW * 32);
     __syncthreads();  // xs staged; full[0] initialised before anyone waits on it
+    // ldsm_x4 weight loads and the matching x reads whenever a chunk lies in
+    // one scale group (always for scale-after): free of bank conflicts
+    const bool tx = SA || gshift >= 7;
     uint32_t xaddr[NT];
     bool xon[NT];
     const XT *xg[NT];
@@ -675,8 +718,8 @@ __global__ void __launch_bounds__(256, 4)
         const int mb = 8 * j + gi;
         xon[j] = mb < m;
         const int mr = xon[j] ? mb : 0;
-        xaddr[j] = smem_u32(xs) + (uint32_t)(mr * xstride + 32 * t) * 2u;
-        xg[j] = x + (size_t)mr * k + 32 * t;
+        xaddr[j] = smem_u32(xs) + (uint32_t)(mr * xstride + (tx ? 8 : 32) * t) * 2u;  // tx: ldsm_x4 layout
+        xg[j] = x + (size_t)mr * k + (tx ? 8 : 32) * t;
     }
     uint4 xb[NT];
 #pragma unroll
@@ -698,29 +741,38 @@ __global__ void __launch_bounds__(256, 4)
             sreg[q][1] = __ldg(scales + (size_t)rb * groups + col);
         }
     }
-    const bool ok = mbar_wait(&full[0], 0);
+    const bool ok = __all_sync(0xffffffffu, mbar_wait(&full[0], 0));  // warp-uniform, as above
     if (ok) {
         auto do_chunk = [&](int q) {
             const int c = warp + q * CW;  // chunk within the row (the stage is the whole row)
-            const uint32_t piece = (uint32_t)(c >> 1) * 2048u + (uint32_t)gi * 128u +
-                                   (uint32_t)(((((c & 1) << 2) + t) ^ (gi & 7)) << 4);
-            const uint4 wa = *reinterpret_cast<const uint4 *>(wst + piece);
-            const uint4 wb = *reinterpret_cast<const uint4 *>(wst + piece + 8 * 128);
+            uint32_t qa[4], qb[4];
+            if (tx) {  // warp-uniform
+                const int lr = lane & 7, lj = lane >> 3;  // ldmatrix row / matrix of this lane
+                const uint32_t a = smem_u32(wst) + (uint32_t)(c >> 1) * 2048u + (uint32_t)lr * 128u +
+                                   (uint32_t)(((((c & 1) << 2) + lj) ^ lr) << 4);
+                ldsm_x4(a, qa);
+                ldsm_x4(a + 8u * 128u, qb);
+            } else {
+                const uint32_t piece = (uint32_t)(c >> 1) * 2048u + (uint32_t)gi * 128u +
+                                       (uint32_t)(((((c & 1) << 2) + t) ^ (gi & 7)) << 4);
+                const uint4 wa = *reinterpret_cast<const uint4 *>(wst + piece);
+                const uint4 wb = *reinterpret_cast<const uint4 *>(wst + piece + 8 * 128);
+                qa[0] = wa.x, qa[1] = wa.y, qa[2] = wa.z, qa[3] = wa.w;
+                qb[0] = wb.x, qb[1] = wb.y, qb[2] = wb.z, qb[3] = wb.w;
+            }
             const int scol = (c * 128 + 32 * t) >> gshift;
             const float sa = STMA ? sst[gi * spr + scol] : sreg[q][0];
             const float sb = STMA ? sst[(gi + 8) * spr + scol] : sreg[q][1];
             const bool in = 128 * c + 32 * t < kp;
-            const uint32_t qa[4] = {wa.x, wa.y, wa.z, wa.w};
-            const uint32_t qb[4] = {wb.x, wb.y, wb.z, wb.w};
             if constexpr (SA) {
-                gemv_chunk_sa<NT, XS, FOLD>(c, qa, qb, in ? sa : 0.0f, in ? sb : 0.0f, xaddr, xon, xg, xb, acc,
+                gemv_chunk_sa<NT, XS, FOLD, true>(c, qa, qb, in ? sa : 0.0f, in ? sb : 0.0f, xaddr, xon, xg, xb, acc,
                                             corr + c * 16 + 2 * t);
             } else {
                 const DqScale dsa = make_dq_scale(in ? sa : 0.0f), dsb = make_dq_scale(in ? sb : 0.0f);
                 if (__all_sync(0xffffffffu, dsa.fast && dsb.fast))
-                    gemv_chunk<XT, NT, XS, true>(c, qa, qb, dsa, dsb, xaddr, xon, xg, xb, acc);
+                    gemv_chunk<XT, NT, XS, true>(c, qa, qb, dsa, dsb, xaddr, xon, xg, xb, acc, tx ? 32 : 8);
                 else
-                    gemv_chunk<XT, NT, XS, false>(c, qa, qb, dsa, dsb, xaddr, xon, xg, xb, acc);
+                    gemv_chunk<XT, NT, XS, false>(c, qa, qb, dsa, dsb, xaddr, xon, xg, xb, acc, tx ? 32 : 8);
             }
         };
         if ((CPW - 1) * CW + warp < nchunks) {
@@ -816,6 +868,9 @@ __global__ void __launch_bounds__(512, 2)
     const uint8_t *wst = smem + grp * stage_pitch;
     const float *sst = reinterpret_cast<const float *>(wst + L::kStageBytes);
     const int row0 = ((int)blockIdx.x + grp * (int)gridDim.x) * 16;
+    // ldsm_x4 weight loads and the matching x reads whenever a chunk lies in
+    // one scale group (always for scale-after): free of bank conflicts
+    const bool tx = SA || gshift >= 7;
     uint32_t xaddr[NT];
     bool xon[NT];
     const XT *xg[NT];
@@ -824,8 +879,8 @@ __global__ void __launch_bounds__(512, 2)
         const int mb = 8 * j + gi;
         xon[j] = mb < m;
         const int mr = xon[j] ? mb : 0;
-        xaddr[j] = smem_u32(xs) + (uint32_t)(mr * xstride + 32 * t) * 2u;
-        xg[j] = x + (size_t)mr * k + 32 * t;
+        xaddr[j] = smem_u32(xs) + (uint32_t)(mr * xstride + (tx ? 8 : 32) * t) * 2u;  // tx: ldsm_x4 layout
+        xg[j] = x + (size_t)mr * k + (tx ? 8 : 32) * t;
     }
     uint4 xb[NT];
 #pragma unroll
@@ -847,29 +902,38 @@ __global__ void __launch_bounds__(512, 2)
             sreg[q][1] = __ldg(scales + (size_t)rb * groups + col);
         }
     }
-    const bool ok = mbar_wait(&full[grp], 0);
+    const bool ok = __all_sync(0xffffffffu, mbar_wait(&full[grp], 0));  // warp-uniform, as above
     if (ok) {
         auto do_chunk = [&](int q) {
             const int c = wg + q * CW;
-            const uint32_t piece = (uint32_t)(c >> 1) * 2048u + (uint32_t)gi * 128u +
-                                   (uint32_t)(((((c & 1) << 2) + t) ^ (gi & 7)) << 4);
-            const uint4 wa = *reinterpret_cast<const uint4 *>(wst + piece);
-            const uint4 wb = *reinterpret_cast<const uint4 *>(wst + piece + 8 * 128);
+            uint32_t qa[4], qb[4];
+            if (tx) {  // warp-uniform
+                const int lr = lane & 7, lj = lane >> 3;  // ldmatrix row / matrix of this lane
+                const uint32_t a = smem_u32(wst) + (uint32_t)(c >> 1) * 2048u + (uint32_t)lr * 128u +
+                                   (uint32_t)(((((c & 1) << 2) + lj) ^ lr) << 4);
+                ldsm_x4(a, qa);
+                ldsm_x4(a + 8u * 128u, qb);
+            } else {
+                const uint32_t piece = (uint32_t)(c >> 1) * 2048u + (uint32_t)gi * 128u +
+                                       (uint32_t)(((((c & 1) << 2) + t) ^ (gi & 7)) << 4);
+                const uint4 wa = *reinterpret_cast<const uint4 *>(wst + piece);
+                const uint4 wb = *reinterpret_cast<const uint4 *>(wst + piece + 8 * 128);
+                qa[0] = wa.x, qa[1] = wa.y, qa[2] = wa.z, qa[3] = wa.w;
+                qb[0] = wb.x, qb[1] = wb.y, qb[2] = wb.z, qb[3] = wb.w;
+            }
             const int scol = (c * 128 + 32 * t) >> gshift;
             const float sa = STMA ? sst[gi * spr + scol] : sreg[q][0];
             const float sb = STMA ? sst[(gi + 8) * spr + scol] : sreg[q][1];
             const bool in = 128 * c + 32 * t < kp;
-            const uint32_t qa[4] = {wa.x, wa.y, wa.z, wa.w};
-            const uint32_t qb[4] = {wb.x, wb.y, wb.z, wb.w};
             if constexpr (SA) {
-                gemv_chunk_sa<NT, XS, FOLD>(c, qa, qb, in ? sa : 0.0f, in ? sb : 0.0f, xaddr, xon, xg, xb, acc,
+                gemv_chunk_sa<NT, XS, FOLD, true>(c, qa, qb, in ? sa : 0.0f, in ? sb : 0.0f, xaddr, xon, xg, xb, acc,
                                             corr + c * 16 + 2 * t);
             } else {
                 const DqScale dsa = make_dq_scale(in ? sa : 0.0f), dsb = make_dq_scale(in ? sb : 0.0f);
                 if (__all_sync(0xffffffffu, dsa.fast && dsb.fast))
-                    gemv_chunk<XT, NT, XS, true>(c, qa, qb, dsa, dsb, xaddr, xon, xg, xb, acc);
+                    gemv_chunk<XT, NT, XS, true>(c, qa, qb, dsa, dsb, xaddr, xon, xg, xb, acc, tx ? 32 : 8);
                 else
-                    gemv_chunk<XT, NT, XS, false>(c, qa, qb, dsa, dsb, xaddr, xon, xg, xb, acc);
+                    gemv_chunk<XT, NT, XS, false>(c, qa, qb, dsa, dsb, xaddr, xon, xg, xb, acc, tx ? 32 : 8);
             }
         };
         if ((CPW - 1) * CW + wg < nchunks) {
@@ -1027,7 +1091,7 @@ inline int tma_gemv_plan(int64_t m, int64_t k, int64_t kp, int g, int nt, int xs
                          int64_t max_pos = 1 << 30) {
     using L = TmaGemvLayout<CW, CPW>;
     if (g < 32 || g > L::kStageCols) return 0;
-    const int64_t xstride = cdiv(kp, 128) * 128 + 8;  // chunks past KP are skipped
+    const int64_t xstride = cdiv(kp, 128) * 128 + gemv_xpad(g);  // chunks past KP are skipped
     const int64_t spr = L::kStageCols / g;
     const size_t sbytes = (size_t)cdiv(16 * spr * 4, 128) * 128;
     const size_t per_stage = (size_t)L::kStageBytes + sbytes + 16;
@@ -1124,7 +1188,7 @@ int launch_gemv_tma(const XT *x, const uint8_t *packed, const float *scales, Out
 constexpr int64_t kTileXs = 16 * 1024;
 
 inline bool gemv_tile_ok(int64_t m, int64_t n, int64_t k, int64_t kp, int g, const uint8_t *packed) {
-    const int64_t xstride = cdiv(kp, 128) * 128 + 8;
+    const int64_t xstride = cdiv(kp, 128) * 128 + gemv_xpad(g);
     const bool xs = m * xstride * 2 <= kTileXs;
     return m <= 16 && g >= 32 && g <= 4096 && kp <= 4096 && aligned(packed, 16) && (kp / 2) % 16 == 0 &&
            n < (1ll << 31) && (xs || (kp == k && kp % 128 == 0));
@@ -1135,7 +1199,7 @@ int launch_gemv_tile(const XT *x, const uint8_t *packed, const float *scales, Ou
                      int64_t k, int64_t kp, int g, int gshift, int prefetch, cudaStream_t st) {
     using L = TmaGemvLayout<8, 4>;
     if (!gemv_tile_ok(m, n, k, kp, g, packed)) return invalid("tile GEMV (config 12) does not take this shape");
-    const int64_t xstride = cdiv(kp, 128) * 128 + 8;
+    const int64_t xstride = cdiv(kp, 128) * 128 + gemv_xpad(g);
     const size_t xbytes = (size_t)(m * xstride) * sizeof(XT);
     const bool xs = (int64_t)xbytes <= kTileXs;
     const size_t sbytes = (size_t)cdiv(16 * (L::kStageCols / g) * 4, 128) * 128;
@@ -1181,7 +1245,7 @@ int launch_gemv_pair(const XT *x, const uint8_t *packed, const float *scales, Ou
                      int64_t k, int64_t kp, int g, int gshift, int prefetch, cudaStream_t st) {
     using L = TmaGemvLayout<8, 4>;
     if (!gemv_pair_ok(m, n, k, kp, g, packed)) return invalid("pair GEMV (config 13) does not take this shape");
-    const int64_t xstride = cdiv(kp, 128) * 128 + 8;
+    const int64_t xstride = cdiv(kp, 128) * 128 + gemv_xpad(g);
     const size_t xbytes = (size_t)(m * xstride) * sizeof(XT);
     const bool xs = (int64_t)xbytes <= kTileXs;
     const size_t sbytes = (size_t)cdiv(16 * (L::kStageCols / g) * 4, 128) * 128;
@@ -1318,9 +1382,10 @@ int launch_gemv(const XT *x, const uint8_t *packed, const float *scales, OutSpec
         (shape == 10 && !tma_gemv_ok<8, 4, 2>(m, k, kp, g, packed)))
         return invalid("TMA GEMV (config %d) does not take this shape", shape);
     if (shape == 11) return invalid("GEMV config 11 is not a launch shape");
-    // Scale-after pays off for M <= 8; with two n-tiles its extra partial
-    // sums cost more registers than the exact path saves.
-    const bool exact = (config & OQ_CONFIG_EXACT_ROUNDING) != 0 || (auto_shape && nt > 1);
+    // Scale-after is the fp16 default up to M = 16 (two n-tiles): with the
+    // conflict-free ldsm_x4 loads it beats the exact rounding there too (45 MB
+    // layer at M = 16: 26.3 vs 30.6 us).
+    const bool exact = (config & OQ_CONFIG_EXACT_ROUNDING) != 0 || (auto_shape && nt > 2);
     const int pf = (config & OQ_CONFIG_STATIC_WEIGHTS) != 0;
     if constexpr (std::is_same<XT, __half>::value) {
         if (!exact && g % 128 == 0)
@@ -1354,7 +1419,7 @@ int launch_gemv_gate(const XT *x, const uint8_t *packed, const float *scales, Ou
                       (shape == 9 && tma_gemv_ok<16, 2>(m, k, kp, g, packed)) ||
                       (shape == 10 && tma_gemv_ok<8, 4, 2>(m, k, kp, g, packed));
     if (!fits) return invalid("SiLU-gate GEMV: the TMA GEMV (config 8, 9 or 10) does not take this shape");
-    const bool exact = (config & OQ_CONFIG_EXACT_ROUNDING) != 0 || (auto_shape && nt > 1);
+    const bool exact = (config & OQ_CONFIG_EXACT_ROUNDING) != 0 || (auto_shape && nt > 2);
     const int pf = (config & OQ_CONFIG_STATIC_WEIGHTS) != 0;
     const int64_t n2 = 2 * n_out;
     auto go = [&](auto sa_tag) -> int {

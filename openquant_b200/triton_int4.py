@@ -45,7 +45,7 @@ def int4_linear(x, packed, scales, out_features, group_size, *, block_m=64, bloc
     "tcgen05"); `out` may supply a preallocated fp32 (M, N) tensor.
     The launch is asynchronous on the current CUDA stream of x's device.
 
-    With fp16 x, M <= 8 and group_size % 128 == 0 the decode GEMV
+    With fp16 x, M <= 16 and group_size % 128 == 0 the decode GEMV
     multiplies x by the exact integer nibbles and applies each fp32 group
     scale to the group's fp32 partial sum (closer to x.(q*s) than the
     reference, and within the parity tolerance of it).  exact_rounding=True
