@@ -91,6 +91,15 @@ __host__ __device__ constexpr size_t gemv_red_bytes(int warps, int nt) { return 
 // Products of fp16 q and x are exact (x / 16 too, unless it falls below the
 // fp16 normal range, |x| < 2^-10) and the tensor core sums them in fp32;
 // y += s * sum per chunk.
+// Scale (row, col) of a stage's scale box.  When a stage row is exactly 128
+// bytes (32 groups: g = 128) the box arrives 128-byte swizzled (16-byte
+// unit u of row r stored at u ^ (r % 8), make_gemv_maps), so the 8 rows a
+// warp reads at one column fall in 8 bank groups instead of one.
+__device__ __forceinline__ float stage_scale(const float *sst, int row, int col, int spr) {
+    if (spr == 32) return sst[row * 32 + ((((col >> 2) ^ (row & 7)) << 2) | (col & 3))];
+    return sst[row * spr + col];
+}
+
 // Four 8x8 b16 matrices from shared memory (ldmatrix): lane L gives the
 // address of row L % 8 of matrix L / 8 and receives, from each matrix j,
 // the 32-bit word L % 4 of row L / 4 in r[j].  On the 128-byte-swizzled
@@ -588,8 +597,8 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW <= 8 ? 2 : 1)
                     qb[0] = wb.x, qb[1] = wb.y, qb[2] = wb.z, qb[3] = wb.w;
                 }
                 const int scol = (cs * 128 + 32 * t) >> gshift;
-                const float sa = STMA ? sst[gi * spr + scol] : sreg[q][0];
-                const float sb = STMA ? sst[(gi + 8) * spr + scol] : sreg[q][1];
+                const float sa = STMA ? stage_scale(sst, gi, scol, spr) : sreg[q][0];
+                const float sb = STMA ? stage_scale(sst, gi + 8, scol, spr) : sreg[q][1];
                 const bool in = 128 * c + 32 * t < kp;
                 if constexpr (SA) {
                     gemv_chunk_sa<NT, XS, FOLD, true>(c, qa, qb, in ? sa : 0.0f, in ? sb : 0.0f, xaddr, xon, xg, xb, acc,
@@ -761,8 +770,8 @@ __global__ void __launch_bounds__(256, 4)
                 qb[0] = wb.x, qb[1] = wb.y, qb[2] = wb.z, qb[3] = wb.w;
             }
             const int scol = (c * 128 + 32 * t) >> gshift;
-            const float sa = STMA ? sst[gi * spr + scol] : sreg[q][0];
-            const float sb = STMA ? sst[(gi + 8) * spr + scol] : sreg[q][1];
+            const float sa = STMA ? stage_scale(sst, gi, scol, spr) : sreg[q][0];
+            const float sb = STMA ? stage_scale(sst, gi + 8, scol, spr) : sreg[q][1];
             const bool in = 128 * c + 32 * t < kp;
             if constexpr (SA) {
                 gemv_chunk_sa<NT, XS, FOLD, true>(c, qa, qb, in ? sa : 0.0f, in ? sb : 0.0f, xaddr, xon, xg, xb, acc,
@@ -922,8 +931,8 @@ __global__ void __launch_bounds__(512, 2)
                 qb[0] = wb.x, qb[1] = wb.y, qb[2] = wb.z, qb[3] = wb.w;
             }
             const int scol = (c * 128 + 32 * t) >> gshift;
-            const float sa = STMA ? sst[gi * spr + scol] : sreg[q][0];
-            const float sb = STMA ? sst[(gi + 8) * spr + scol] : sreg[q][1];
+            const float sa = STMA ? stage_scale(sst, gi, scol, spr) : sreg[q][0];
+            const float sb = STMA ? stage_scale(sst, gi + 8, scol, spr) : sreg[q][1];
             const bool in = 128 * c + 32 * t < kp;
             if constexpr (SA) {
                 gemv_chunk_sa<NT, XS, FOLD, true>(c, qa, qb, in ? sa : 0.0f, in ? sb : 0.0f, xaddr, xon, xg, xb, acc,
@@ -1128,7 +1137,8 @@ int make_gemv_maps(const uint8_t *packed, const float *scales, int64_t n, int64_
     if (*stma) {
         rc = make_tensor_map_2d(smap, scales, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)groups, (uint64_t)n,
                                 (uint64_t)(groups * 4), (uint32_t)(L::kStageCols / g), 16,
-                                CU_TENSOR_MAP_SWIZZLE_NONE);
+                                (L::kStageCols / g) * 4 == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                                                 : CU_TENSOR_MAP_SWIZZLE_NONE);  // see stage_scale
         if (rc != OQ_OK) return rc;
     } else {
         *smap = *wmap;  // unused
