@@ -69,7 +69,8 @@ typedef void *oq_stream_t; /* a cudaStream_t */
  * fp16 GEMV with group_size % 128 == 0 multiplies x by the exact integer
  * nibbles and applies each fp32 group scale to the group's fp32 partial
  * sum -- closer to x.(q*s) than the reference, within the parity tolerance
- * of it, and ~2.5x fewer instructions per weight. */
+ * of it, and ~2.5x fewer instructions per weight.  The automatic launch
+ * shape (config 0) does so up to M = 16. */
 #define OQ_CONFIG_EXACT_ROUNDING 16
 
 /* oq_int4_linear `config` flag: the packed weights and scales are static --
@@ -194,7 +195,9 @@ OQ_API int oq_dequant_int4_group(const uint8_t *packed, const float *scales,
  *             (8,4,4), and 8, 9, 10 the TMA-fed kernel with 8 or 16
  *             consumer warps and one CTA per SM, or 8 warps and two CTAs per
  *             SM (M <= 16), 12 one CTA per 16-row tile with four CTAs per SM
- *             (M <= 16, K <= 4096) -- only the fp32 summation order changes;
+ *             (M <= 16, K <= 4096), 13 one 16-warp CTA per SM owning two
+ *             16-row tiles (M <= 16, K <= 4096, at most two tiles per SM) --
+ *             only the fp32 summation order changes;
  *             `openquant tune` picks it.  | OQ_CONFIG_EXACT_ROUNDING,
  *             | OQ_CONFIG_STATIC_WEIGHTS: see above.
  */
