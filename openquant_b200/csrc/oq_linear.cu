@@ -91,13 +91,16 @@ __host__ __device__ constexpr size_t gemv_red_bytes(int warps, int nt) { return 
 // Products of fp16 q and x are exact (x / 16 too, unless it falls below the
 // fp16 normal range, |x| < 2^-10) and the tensor core sums them in fp32;
 // y += s * sum per chunk.
-// Scale (row, col) of a stage's scale box.  When a stage row is exactly 128
+// Scales (rows g and g + 8, col) of a stage's scale box.  When a stage row is exactly 128
 // bytes (32 groups: g = 128) the box arrives 128-byte swizzled (16-byte
 // unit u of row r stored at u ^ (r % 8), make_gemv_maps), so the 8 rows a
 // warp reads at one column fall in 8 bank groups instead of one.
-__device__ __forceinline__ float stage_scale(const float *sst, int row, int col, int spr) {
-    if (spr == 32) return sst[row * 32 + ((((col >> 2) ^ (row & 7)) << 2) | (col & 3))];
-    return sst[row * spr + col];
+// Rows g and g + 8 share (row % 8), hence the swizzled column: both scales
+// of a lane come from one index computation.
+__device__ __forceinline__ void stage_scales(const float *sst, int gi, int col, int spr, float &sa, float &sb) {
+    const int c = spr == 32 ? ((((col >> 2) ^ (gi & 7)) << 2) | (col & 3)) : col;
+    sa = sst[gi * spr + c];
+    sb = sst[(gi + 8) * spr + c];
 }
 
 // Four 8x8 b16 matrices from shared memory (ldmatrix): lane L gives the
@@ -141,35 +144,57 @@ __device__ __forceinline__ uint4 sa_perm_x(uint4 v) {
 // order: with KP % 128 == 0, thread i stages vector i % (KP/8) of row
 // i / (KP/8), so a chunk's 16 vectors lie in 16 aligned lanes and a
 // shuffle tree sums them.  All threads of the block call it.
-template <typename XT, bool SA, bool FOLD>
+template <typename XT, bool SA, bool FOLD, int U = 1>
 __device__ __forceinline__ void gemv_stage_x(const XT *__restrict__ x, XT *xs, float *corr, int m, int k, int kp,
                                              int xstride, int nthreads) {
+    // U vectors per thread per pass, their loads issued first: a pass waits
+    // for one round trip to L2 instead of U (the persistent TMA kernel stages
+    // 8-32 vectors per thread at M = 4-16, K = 4096; the register-capped tile
+    // and pair kernels use U = 1).
     if (!FOLD) {
-        const int rowv = xstride / 8, kv = k / 8;
-        for (int i = threadIdx.x; i < m * rowv; i += nthreads) {
-            const int r = i / rowv, c = i - r * rowv;
-            uint4 v = c < kv ? __ldg(reinterpret_cast<const uint4 *>(x) + (size_t)r * kv + c) : make_uint4(0, 0, 0, 0);
-            if (SA) v = sa_perm_x(v);
-            reinterpret_cast<uint4 *>(xs)[i] = v;
+        const int rowv = xstride / 8, kv = k / 8, total = m * rowv;
+        for (int i0 = threadIdx.x; i0 < total; i0 += U * nthreads) {
+            uint4 v[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int i = i0 + u * nthreads;
+                const int r = i / rowv, c = i - r * rowv;
+                v[u] = i < total && c < kv ? __ldg(reinterpret_cast<const uint4 *>(x) + (size_t)r * kv + c)
+                                           : make_uint4(0, 0, 0, 0);
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int i = i0 + u * nthreads;
+                if (i < total) reinterpret_cast<uint4 *>(xs)[i] = SA ? sa_perm_x(v[u]) : v[u];
+            }
         }
     } else {
         const int kv8 = kp / 8, kv = k / 8, total = m * kv8;
-        for (int i0 = (int)threadIdx.x - (int)(threadIdx.x & 31); i0 < total; i0 += nthreads) {
-            const int i = i0 + (int)(threadIdx.x & 31);
-            const bool live = i < total;
-            const int r = live ? i / kv8 : 0, cv = live ? i - r * kv8 : 0;
-            uint4 v = make_uint4(0, 0, 0, 0);
-            if (live && cv < kv) v = __ldg(reinterpret_cast<const uint4 *>(x) + (size_t)r * kv + cv);
-            v = sa_perm_x(v);
-            if (live) reinterpret_cast<uint4 *>(xs)[r * (xstride / 8) + cv] = v;
-            const float2 f0 = __half22float2(*reinterpret_cast<const __half2 *>(&v.x));
-            const float2 f1 = __half22float2(*reinterpret_cast<const __half2 *>(&v.y));
-            const float2 f2 = __half22float2(*reinterpret_cast<const __half2 *>(&v.z));
-            const float2 f3 = __half22float2(*reinterpret_cast<const __half2 *>(&v.w));
-            float t = 1032.0f * ((f0.x + f0.y) + (f1.x + f1.y)) + 1152.0f * ((f2.x + f2.y) + (f3.x + f3.y));
+        for (int b0 = (int)threadIdx.x - (int)(threadIdx.x & 31); b0 < total; b0 += U * nthreads) {
+            uint4 v[U];
 #pragma unroll
-            for (int o = 8; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
-            if (live && (cv & 15) == 0) corr[(cv >> 4) * 16 + r] = t;
+            for (int u = 0; u < U; ++u) {
+                const int i = b0 + u * nthreads + (int)(threadIdx.x & 31);
+                const int r = i < total ? i / kv8 : 0, cv = i < total ? i - r * kv8 : 0;
+                v[u] = make_uint4(0, 0, 0, 0);
+                if (i < total && cv < kv) v[u] = __ldg(reinterpret_cast<const uint4 *>(x) + (size_t)r * kv + cv);
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int i = b0 + u * nthreads + (int)(threadIdx.x & 31);
+                const bool live = i < total;
+                const int r = live ? i / kv8 : 0, cv = live ? i - r * kv8 : 0;
+                const uint4 w = sa_perm_x(v[u]);
+                if (live) reinterpret_cast<uint4 *>(xs)[r * (xstride / 8) + cv] = w;
+                const float2 f0 = __half22float2(*reinterpret_cast<const __half2 *>(&w.x));
+                const float2 f1 = __half22float2(*reinterpret_cast<const __half2 *>(&w.y));
+                const float2 f2 = __half22float2(*reinterpret_cast<const __half2 *>(&w.z));
+                const float2 f3 = __half22float2(*reinterpret_cast<const __half2 *>(&w.w));
+                float t = 1032.0f * ((f0.x + f0.y) + (f1.x + f1.y)) + 1152.0f * ((f2.x + f2.y) + (f3.x + f3.y));
+#pragma unroll
+                for (int o = 8; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+                if (live && (cv & 15) == 0) corr[(cv >> 4) * 16 + r] = t;
+            }
         }
     }
 }
@@ -526,7 +551,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW <= 8 ? 2 : 1)
     const int gi = lane >> 2, t = lane & 3;
     asm volatile("griddepcontrol.wait;" ::: "memory");
     if (XS) {
-        gemv_stage_x<XT, SA, FOLD>(x, xs, corr, m, k, kp, xstride, CW * 32);
+        gemv_stage_x<XT, SA, FOLD, 4>(x, xs, corr, m, k, kp, xstride, CW * 32);
         asm volatile("bar.sync 1, %0;" ::"r"(CW * 32) : "memory");
     }
     // ldsm_x4 weight loads and the matching x reads whenever a chunk lies in
@@ -597,8 +622,11 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW <= 8 ? 2 : 1)
                     qb[0] = wb.x, qb[1] = wb.y, qb[2] = wb.z, qb[3] = wb.w;
                 }
                 const int scol = (cs * 128 + 32 * t) >> gshift;
-                const float sa = STMA ? stage_scale(sst, gi, scol, spr) : sreg[q][0];
-                const float sb = STMA ? stage_scale(sst, gi + 8, scol, spr) : sreg[q][1];
+                float sa, sb;
+                if (STMA)
+                    stage_scales(sst, gi, scol, spr, sa, sb);
+                else
+                    sa = sreg[q][0], sb = sreg[q][1];
                 const bool in = 128 * c + 32 * t < kp;
                 if constexpr (SA) {
                     gemv_chunk_sa<NT, XS, FOLD, true>(c, qa, qb, in ? sa : 0.0f, in ? sb : 0.0f, xaddr, xon, xg, xb, acc,
@@ -770,8 +798,11 @@ __global__ void __launch_bounds__(256, 4)
                 qb[0] = wb.x, qb[1] = wb.y, qb[2] = wb.z, qb[3] = wb.w;
             }
             const int scol = (c * 128 + 32 * t) >> gshift;
-            const float sa = STMA ? stage_scale(sst, gi, scol, spr) : sreg[q][0];
-            const float sb = STMA ? stage_scale(sst, gi + 8, scol, spr) : sreg[q][1];
+            float sa, sb;
+            if (STMA)
+                stage_scales(sst, gi, scol, spr, sa, sb);
+            else
+                sa = sreg[q][0], sb = sreg[q][1];
             const bool in = 128 * c + 32 * t < kp;
             if constexpr (SA) {
                 gemv_chunk_sa<NT, XS, FOLD, true>(c, qa, qb, in ? sa : 0.0f, in ? sb : 0.0f, xaddr, xon, xg, xb, acc,
@@ -931,8 +962,11 @@ __global__ void __launch_bounds__(512, 2)
                 qb[0] = wb.x, qb[1] = wb.y, qb[2] = wb.z, qb[3] = wb.w;
             }
             const int scol = (c * 128 + 32 * t) >> gshift;
-            const float sa = STMA ? stage_scale(sst, gi, scol, spr) : sreg[q][0];
-            const float sb = STMA ? stage_scale(sst, gi + 8, scol, spr) : sreg[q][1];
+            float sa, sb;
+            if (STMA)
+                stage_scales(sst, gi, scol, spr, sa, sb);
+            else
+                sa = sreg[q][0], sb = sreg[q][1];
             const bool in = 128 * c + 32 * t < kp;
             if constexpr (SA) {
                 gemv_chunk_sa<NT, XS, FOLD, true>(c, qa, qb, in ? sa : 0.0f, in ? sb : 0.0f, xaddr, xon, xg, xb, acc,
