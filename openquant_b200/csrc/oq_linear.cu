@@ -1172,7 +1172,7 @@ int make_gemv_maps(const uint8_t *packed, const float *scales, int64_t n, int64_
         rc = make_tensor_map_2d(smap, scales, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)groups, (uint64_t)n,
                                 (uint64_t)(groups * 4), (uint32_t)(L::kStageCols / g), 16,
                                 (L::kStageCols / g) * 4 == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
-                                                                 : CU_TENSOR_MAP_SWIZZLE_NONE);  // see stage_scale
+                                                                 : CU_TENSOR_MAP_SWIZZLE_NONE);  // see stage_scales
         if (rc != OQ_OK) return rc;
     } else {
         *smap = *wmap;  // unused
