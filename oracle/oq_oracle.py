@@ -135,7 +135,9 @@ def round_to_dtype(a, dtype):
     bf16 uses the same rounding on the top 16 bits of the fp32 pattern."""
     a = np.asarray(a, dtype=np.float32)
     if dtype in ("f16", "float16", np.float16):
-        return a.astype(np.float16).astype(np.float32)
+        # beyond the fp16 range the value becomes +-inf, as torch's .half() does
+        with np.errstate(over="ignore"):
+            return a.astype(np.float16).astype(np.float32)
     if dtype in ("bf16", "bfloat16"):
         u = a.view(np.uint32).astype(np.uint64)
         lsb = (u >> 16) & 1
