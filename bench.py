@@ -43,6 +43,7 @@ M, K, N, G = 1, 4096, 4096, 128
 KP = ((K + G - 1) // G) * G
 ALG_BYTES = N * KP // 2 + N * (KP // G) * 4 + M * K * 2 + M * N * 4  # 8,937,472
 COPIES = 64
+ONE_GRAPH_MAX = 8192  # up to this many warm-up + timed launches, one graph each
 L2_BYTES = 126 * 1024 * 1024
 WORKLOAD = "int4_gemv_m1_k4096_n4096_g128_fp16"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
@@ -129,6 +130,50 @@ class ClockSampler:
             "reasons": sorted(reasons),
             "samples": len(sm),
         }
+
+
+def headline_config(world):
+    """`config` of the headline line, the same for both arms."""
+    return {
+        "workload": WORKLOAD,
+        "m": M, "k": K, "n": N, "group_size": G,
+        "weights": f"{COPIES} distinct INT4 copies rotated ({COPIES * ALG_BYTES / 1e6:.0f} MB > L2)",
+        "l2": "inputs larger than L2 (weight-copy rotation), no flush",
+        "launch": "CUDA graphs of back-to-back launches (programmatic dependent launch): up to 8 of the W "
+                  "warm-up launches eagerly, then behind a device-side sleep (so the host's submission is off the "
+                  "clock) the other warm-up launches, the start event, the K timed launches (one graph up to "
+                  f"{ONE_GRAPH_MAX} launches), the end event",
+        "static_weights": "weights quantized at setup and synchronized, so each launch streams them "
+                          "while the previous one drains (OQ_CONFIG_STATIC_WEIGHTS); x and y stay ordered",
+        "parallelism": f"dp{world} (each rank streams its own weight copies)",
+    }
+
+
+def summarize(line):
+    """Compact figures of the headline and of every `also` line."""
+    r3 = lambda v: None if v is None else round(float(v), 3)  # noqa: E731
+    out = {"headline_gbs": r3(line["value"] / line["n_gpus"]), "headline_frac": r3(line["roofline"]["frac"]),
+           "e2e_gbs": r3(line["e2e"]["value"])}
+    for a in line.get("also", []):
+        wl = a.get("workload", "")
+        if wl.startswith("int4_gemv_llama2"):
+            out["decode_set"] = {f"m{m}": {"gbs": r3(v["gbs"]), "frac": r3(v["frac"])} for m, v in a["by_m"].items()}
+        elif wl.startswith("int4_gemm_llama3"):
+            out["prefill_set"] = {c: {"tflops": r3(v["tflops"]), "frac": r3(v["frac"])}
+                                  for c, v in a["by_case"].items()}
+        elif wl.startswith("int4_gemm_m2048"):
+            out["gemm_m2048"] = {"tflops": r3(a["value"]), "frac": r3(a["roofline"]["frac"])}
+        elif wl.startswith("int8_gemm"):
+            out["w8a8_m2048"] = {"tops": r3(a["value"]), "frac": r3(a["roofline"]["frac"])}
+        elif wl.startswith("bulk_quant"):
+            out["bulk_int4_g128"] = {"gbs": r3(a["value"]), "frac": r3(a["roofline"]["frac"])}
+        elif wl.startswith("int4_linear_sharded"):
+            out["sharded"] = {c: {k: r3(v[k]) for k in ("tflops", "us", "efficiency_vs_1gpu", "allgather_ms")
+                                  if k in v} for c, v in a["by_case"].items()}
+        elif wl.startswith("cpu_path_1024"):
+            out["cpu_path_1024"] = {f: {"gpu_ms": r3(v["gpu_ms"]), "cpu_ms": r3(v["cpu_ms"]),
+                                        "rel_weight_err": r3(v["rel_weight_err"])} for f, v in a["formats"].items()}
+    return out
 
 
 # ---------------------------------------------------------- CPU side --
@@ -232,7 +277,7 @@ def run_reference(args):
         "vs_baseline": None,
         "dtype": "f16",
         "data": "synthetic",
-        "config": {"workload": WORKLOAD, "sample_rows_per_step": rows, "l2": "host run"},
+        "config": headline_config(int(os.environ.get("WORLD_SIZE", "1"))),
         "cpu_baseline": {
             "value": value,
             "unit": UNIT,
@@ -289,13 +334,7 @@ def measure_gemm(dev, peaks, steps=10, warmup=3):
         launch(steps, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
     graph.replay()
     torch.cuda.synchronize()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):
-        start.record(stream)
-        graph.replay()
-        end.record(stream)
-    torch.cuda.synchronize()
-    ms = start.elapsed_time(end) / steps
+    ms = _device_timed(stream, graph.replay, steps)
     tflops = 2.0 * m * n * k / (ms / 1e3) / 1e12
     # spot check against the exactly-rounded weights on sampled columns
     from oq_oracle import dequantize_int4_groupwise as deq, round_to_dtype
@@ -305,7 +344,8 @@ def measure_gemm(dev, peaks, steps=10, warmup=3):
                             (len(rows), k), g), "bf16")
     ref = x.double() @ torch.from_numpy(wr).to(dev).double().T
     rel = ((y[:, rows].double() - ref).norm() / ref.norm()).item()
-    assert rel < 1e-3, rel
+    mab = (y[:, rows].double() - ref).abs().max().item()
+    assert rel <= 1e-3 and mab <= 2e-2, (rel, mab)
     del graph
     return {
         "metric": "INT4 dequant-GEMM TFLOP/s at M=2048",
@@ -326,6 +366,7 @@ def measure_gemm(dev, peaks, steps=10, warmup=3):
         },
         "gpu_launches": steps,
         "check_rel_l2": rel,
+        "check_max_abs": mab,
     }
 
 
@@ -349,7 +390,7 @@ def measure_prefill_set(dev, peaks, ms_=(512, 2048, 8192), steps=5, warmup=2):
     lib = nat.load()
     g = 128
     stream = torch.cuda.Stream(device=dev)
-    cases, rel_worst, launches = {}, 0.0, 0
+    cases, rel_worst, abs_worst, launches = {}, 0.0, 0.0, 0
     for si, (name, k, n) in enumerate(PREFILL_SHAPES):
         gen = torch.Generator(device=dev).manual_seed(700 + si)
         w = torch.randn(n, k, generator=gen, device=dev).mul_(0.02).to(torch.bfloat16)
@@ -381,20 +422,15 @@ def measure_prefill_set(dev, peaks, ms_=(512, 2048, 8192), steps=5, warmup=2):
                 launch(steps, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
             graph.replay()
             torch.cuda.synchronize()
-            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            with torch.cuda.stream(stream):
-                start.record(stream)
-                graph.replay()
-                end.record(stream)
-            torch.cuda.synchronize()
+            ms = _device_timed(stream, graph.replay, steps)
             del graph
             launches += warmup + 2 * steps
-            ms = start.elapsed_time(end) / steps
             tflops = 2.0 * m * n * k / (ms / 1e3) / 1e12
             ref = x.double() @ wr.double().T
             rel = ((y[:, rows].double() - ref).norm() / ref.norm()).item()
-            assert rel < 1e-3, (name, m, rel)
-            rel_worst = max(rel_worst, rel)
+            mab = (y[:, rows].double() - ref).abs().max().item()
+            assert rel <= 1e-3 and mab <= 2e-2, (name, m, rel, mab)
+            rel_worst, abs_worst = max(rel_worst, rel), max(abs_worst, mab)
             cases[f"{name}_m{m}_k{k}_n{n}"] = {"ms": ms, "tflops": tflops, "frac": tflops / peaks["bf16_tflops"],
                                               "frac_of_sustained": tflops / peaks["bf16_tflops_sustained"]}
             del x, y
@@ -409,6 +445,7 @@ def measure_prefill_set(dev, peaks, ms_=(512, 2048, 8192), steps=5, warmup=2):
         "by_case": cases,
         "gpu_launches": launches,
         "check_rel_l2": rel_worst,
+        "check_max_abs": abs_worst,
     }
 
 
@@ -444,7 +481,7 @@ def measure_decode_layers(dev, peaks, ms_=(1, 4, 16), sets=3, steps=200, warmup=
         layers.append((name, k, n, copies, n * k // 2 + n * (k // g) * 4))
     stream = torch.cuda.Stream(device=dev)
     out = {}
-    rel_worst = 0.0
+    rel_worst, abs_worst = 0.0, 0.0
     launches = 0
     for m in ms_:
         gen = torch.Generator(device=dev).manual_seed(900 + m)
@@ -472,14 +509,9 @@ def measure_decode_layers(dev, peaks, ms_=(1, 4, 16), sets=3, steps=200, warmup=
                 run(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream), seq)
             graph.replay()
             torch.cuda.synchronize()
-            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            with torch.cuda.stream(stream):
-                start.record(stream)
-                graph.replay()
-                end.record(stream)
-            torch.cuda.synchronize()
+            ms = _device_timed(stream, graph.replay, 1)
             del graph
-            return start.elapsed_time(end) * 1e3
+            return ms * 1e3
 
         step_seq = [calls[li][s % sets] for s in range(steps) for li in range(len(layers))]
         step_us = timed(step_seq) / steps
@@ -500,8 +532,9 @@ def measure_decode_layers(dev, peaks, ms_=(1, 4, 16), sets=3, steps=200, warmup=
         wref = dequantize_int4_groupwise(Groupwise4(p, sc, (4096, 4096), g)).half().double()
         yref = xs[1].double() @ wref.T
         rel = ((ys[1].double() - yref).norm() / yref.norm()).item()
-        assert rel < 1e-3, rel
-        rel_worst = max(rel_worst, rel)
+        mab = (ys[1].double() - yref).abs().max().item()
+        assert rel <= 1e-3 and mab <= 2e-2, (rel, mab)
+        rel_worst, abs_worst = max(rel_worst, rel), max(abs_worst, mab)
         gbs = step_bytes / step_us / 1e3
         out[str(m)] = {"us_per_step": step_us, "gbs": gbs, "frac": gbs / peaks["hbm_gbs"], "layers": per_layer}
     del layers
@@ -516,6 +549,7 @@ def measure_decode_layers(dev, peaks, ms_=(1, 4, 16), sets=3, steps=200, warmup=
         "launch": "CUDA graph of back-to-back launches (programmatic dependent launch), static weights",
         "gpu_launches": launches,
         "check_rel_l2": rel_worst,
+        "check_max_abs": abs_worst,
     }
 
 
@@ -558,14 +592,8 @@ def measure_w8a8(dev, peaks, steps=10, warmup=3):
         launch(steps, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
     graph.replay()
     torch.cuda.synchronize()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):
-        start.record(stream)
-        graph.replay()
-        end.record(stream)
-    torch.cuda.synchronize()
+    ms = _device_timed(stream, graph.replay, steps)
     del graph
-    ms = start.elapsed_time(end) / steps
     tops = 2.0 * m * n * k / (ms / 1e3) / 1e12
     # exact check on sampled columns: the int32 sums are exact, the epilogue rounds three times
     cols = torch.arange(0, n, 1021, device=dev)
@@ -586,6 +614,106 @@ def measure_w8a8(dev, peaks, steps=10, warmup=3):
                      "algorithmic_ops_per_launch": 2 * m * n * k},
         "gpu_launches": steps,
         "check_max_rel_err": rel,
+    }
+
+
+def measure_cpu_path_1024(dev, peaks, steps=50, warmup=5):
+    """The reference's CPU NumPy case (quantization.py:14-82, benchmark.py:7-38)
+    on the GPU: W 1024x1024 fp32 ~ N(0, 0.02) and x 16x1024 ~ N(0, 1) from
+    np.random.default_rng(0); per format (INT8 per-row, packed INT4 per-row)
+    one step = quantize -> dequantize -> x @ W_hat^T (the matmul in fp32,
+    TF32 off), CUDA-graph replays timed with CUDA events.  The quantized bytes
+    and scales must equal the oracle's; the reported errors are the
+    reference's weight error ||W_hat - W|| / ||W|| and the output's relative
+    error against x @ W^T.  The CPU side times the oracle's NumPy restatement of
+    the same three steps on the host (NumPy ufuncs on one core, the matmul on
+    the BLAS threads)."""
+    import ctypes
+
+    import torch
+
+    from oq_oracle import dequantize as odeq, quantize as oquant
+    from openquant_b200 import _native as nat
+
+    lib = nat.load()
+    rng = np.random.default_rng(0)
+    w = rng.normal(0, 0.02, (1024, 1024)).astype(np.float32)
+    x = rng.normal(0, 1, (16, 1024)).astype(np.float32)
+    n, k = w.shape
+    wt, xt = torch.from_numpy(w).to(dev), torch.from_numpy(x).to(dev)
+    yref = x.astype(np.float64) @ w.astype(np.float64).T
+    stream = torch.cuda.Stream(device=dev)
+    tf32 = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    formats, launches = {}, 0
+    try:
+        for bits in (8, 4):
+            q = torch.empty(n * k if bits == 8 else (n * k + 1) // 2, dtype=torch.uint8, device=dev)
+            sc = torch.empty(n, device=dev)
+            wd = torch.empty(n, k, device=dev)
+            y = torch.empty(16, n, device=dev)
+            torch.cuda.synchronize()
+
+            def step(h):
+                if bits == 8:
+                    nat.check(lib.oq_quant_int8_rowwise(ctypes.c_void_p(wt.data_ptr()), nat.OQ_F32, n, k,
+                                                        ctypes.c_void_p(q.data_ptr()), ctypes.c_void_p(sc.data_ptr()), h))
+                    nat.check(lib.oq_dequant_int8_rowwise(ctypes.c_void_p(q.data_ptr()), ctypes.c_void_p(sc.data_ptr()),
+                                                          n, k, ctypes.c_void_p(wd.data_ptr()), h))
+                else:
+                    nat.check(lib.oq_quant_int4_rowwise(ctypes.c_void_p(wt.data_ptr()), nat.OQ_F32, n, k,
+                                                        ctypes.c_void_p(q.data_ptr()), ctypes.c_void_p(sc.data_ptr()), h))
+                    nat.check(lib.oq_dequant_int4_rowwise(ctypes.c_void_p(q.data_ptr()), ctypes.c_void_p(sc.data_ptr()),
+                                                          n, k, ctypes.c_void_p(wd.data_ptr()), h))
+                torch.matmul(xt, wd.T, out=y)
+
+            with torch.cuda.stream(stream):
+                for _ in range(warmup):
+                    step(ctypes.c_void_p(stream.cuda_stream))
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph, stream=stream):
+                    for _ in range(steps):
+                        step(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+            torch.cuda.synchronize()
+            gpu_ms = _device_timed(stream, graph.replay, steps)
+            del graph
+            launches += 3 * (warmup + steps)
+            d_ref, s_ref = oquant(w, bits)
+            got = q.cpu().numpy()
+            assert np.array_equal(got.view(np.int8) if bits == 8 else got, d_ref.reshape(-1)), bits
+            assert np.array_equal(sc.cpu().numpy().view(np.uint32), s_ref.reshape(-1).view(np.uint32)), bits
+            wd_np = wd.cpu().numpy()
+            assert np.array_equal(wd_np.view(np.uint32), odeq(d_ref, s_ref, bits, (n, k)).view(np.uint32)), bits
+            rel_w = float(np.linalg.norm(wd_np - w) / np.linalg.norm(w))
+            rel_y = float(np.linalg.norm(y.cpu().numpy() - yref) / np.linalg.norm(yref))
+            # the same three steps on the host (oracle restatement of the reference's NumPy code)
+            times = []
+            for _ in range(7):
+                t0 = time.perf_counter()
+                d_, s_ = oquant(w, bits)
+                _ = x @ odeq(d_, s_, bits, (n, k)).T
+                times.append(time.perf_counter() - t0)
+            cpu_ms = statistics.median(times) * 1e3
+            formats[f"int{bits}_rowwise"] = {"gpu_ms": gpu_ms, "gpu_mweights_s": n * k / gpu_ms / 1e3,
+                                             "cpu_ms": cpu_ms, "cpu_mweights_s": n * k / cpu_ms / 1e3,
+                                             "rel_weight_err": rel_w, "rel_output_err": rel_y}
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = tf32
+    head = formats["int4_rowwise"]
+    return {
+        "metric": "CPU-path case on the GPU: quantize + dequantize + x[16,1024] @ W_hat^T per second, "
+                  "W 1024x1024 fp32 N(0,0.02) seed 0",
+        "workload": "cpu_path_1024x1024_int8_int4",
+        "value": head["gpu_mweights_s"],
+        "unit": "Mweights/s",
+        "value_is": "INT4 per-row; INT8 and INT4 in formats",
+        "formats": formats,
+        "gpu_launches": launches,
+        "launch": "CUDA graph of the three steps (quantize and dequantize kernels, cuBLAS fp32 matmul, TF32 off)",
+        "check": "quantized bytes, scales and dequantized weights bit-exact vs the oracle",
+        "cpu_baseline": {"value": head["cpu_mweights_s"], "unit": "Mweights/s", "cores": 1, "kind": "port",
+                         "sample": "the whole case, median of 7 (NumPy ufuncs on one core; the 16x1024x1024 "
+                                   "matmul on the BLAS threads)"},
     }
 
 
@@ -777,52 +905,227 @@ def measure_bulk_quant(dev, world, rank, peaks, layers=BULK_LAYERS):
     return entry
 
 
-def measure_sharded_gemm(dev, world, rank, peaks, steps=10, warmup=3):
-    """Column-sharded prefill layer across the ranks: M = 2048, K = 8192,
-    N = 28672 split into contiguous row blocks, each rank's tcgen05 GEMM slice
-    then an NCCL all-gather of the (M, N/P) fp32 slices.  Time = max over
-    ranks of the event-timed steps; value = whole-layer TFLOP/s."""
+SHARD_K, SHARD_N = 8192, 28672  # Llama-3-70B MLP gate/up projection
+
+
+def _device_timed(stream, body, steps, host_us_per_step=0.0):
+    """ms per step of `body()` (enqueues one step on `stream`) over `steps`
+    steps, timed with CUDA events on `stream`.  A device-side sleep is
+    enqueued ahead of the start event so that the host has queued the steps
+    before the GPU reaches them: the events then bracket device work only."""
+    import torch
+
+    cycles = int(2e6 + 2e3 * host_us_per_step * steps)  # ~1 ms + the host's enqueue time at ~2 GHz
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        torch.cuda._sleep(cycles)
+        start.record(stream)
+        body()
+        end.record(stream)
+    torch.cuda.synchronize()
+    return start.elapsed_time(end) / steps
+
+
+def upload_graph(graph, stream):
+    """Uploads an instantiated CUDA graph's work to the device
+    (cuGraphUpload) on `stream`, so that its first replay -- inside a timed
+    region -- does not carry the upload."""
+    import ctypes
+
+    cuda = ctypes.CDLL("libcuda.so.1")
+    rc = cuda.cuGraphUpload(ctypes.c_void_p(graph.raw_cuda_graph_exec()), ctypes.c_void_p(stream.cuda_stream))
+    if rc != 0:
+        raise RuntimeError(f"cuGraphUpload failed ({rc})")
+
+
+def _max_over_ranks(v, dev, world):
     import torch
     import torch.distributed as dist
 
-    from openquant_b200.groupwise import quantize_int4_groupwise
-    from openquant_b200.sharding import ShardedInt4Linear, shard_bounds
-
-    m, k, n, g = 2048, 8192, 28672, 128
-    start, end = shard_bounds(n, world, rank)
-    gen = torch.Generator(device=dev).manual_seed(500 + rank)
-    w = torch.randn(end - start, k, generator=gen, device=dev).mul_(0.02).to(torch.bfloat16)
-    local = quantize_int4_groupwise(w, g)
-    del w
-    gx = torch.Generator(device=dev).manual_seed(501)
-    x = torch.randn(m, k, generator=gx, device=dev).to(torch.bfloat16)
-    lin = ShardedInt4Linear(local, n)
-    for _ in range(warmup):
-        y = lin(x)
-    torch.cuda.synchronize()
-    dist.barrier()
-    start_ev, end_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start_ev.record()
-    for _ in range(steps):
-        y = lin(x)
-    end_ev.record()
-    torch.cuda.synchronize()
-    ms = start_ev.elapsed_time(end_ev) / steps
-    t = torch.tensor([ms], device=dev)
+    if world == 1:
+        return v
+    t = torch.tensor([v], device=dev, dtype=torch.float64)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t.item())
-    assert y.shape == (m, n)
-    tflops = 2.0 * m * n * k / (ms / 1e3) / 1e12
+    return float(t.item())
+
+
+def measure_sharded(dev, world, rank, peaks, prefill_ms=(2048, 8192), decode_ms=(1, 16)):
+    """The N-column-sharded Llama-3-70B gate/up layer (K = 8192, N = 28672,
+    INT4 g = 128) over the ranks, each owning N/P contiguous weight rows:
+
+    * p2p  -- the fused path: each rank's kernels store their (M, N/P) slice
+              straight into every rank's (M, N) output over NVLink, then a
+              bounded flag barrier (ShardedInt4Linear mode "p2p"), fp32 output
+              (the reference's) and bf16 output;
+    * nccl -- the local slice, then an NCCL all-gather and a relayout copy.
+
+    Prefill at M = 2048 and 8192 (bf16 x) in TFLOP/s of the whole layer,
+    decode at M = 1 and 16 (fp16 x) in µs per call.  Each case is timed with
+    CUDA events over back-to-back steps (p2p: one CUDA graph of the steps),
+    max over ranks, and compared with the same full layer on one GPU
+    (`efficiency_vs_1gpu` = t_1gpu / (P * t_P)).  Every rank checks sampled
+    columns spanning all shards against the oracle's exactly-rounded weights
+    (rel-L2 <= 1e-3 and max-abs <= 2e-2); the bf16 output must equal the fp32
+    output rounded once."""
+    import torch
+    import torch.distributed as dist
+
+    from oq_oracle import dequantize_int4_groupwise as deq, round_to_dtype
+    from openquant.triton_int4 import int4_linear
+    from openquant_b200.groupwise import Groupwise4, quantize_int4_groupwise
+    from openquant_b200.sharding import ShardedInt4Linear, shard_bounds, shard_groupwise
+
+    k, n, g = SHARD_K, SHARD_N, 128
+    gen = torch.Generator(device=dev).manual_seed(500)  # the same layer on every rank
+    w = torch.randn(n, k, generator=gen, device=dev).mul_(0.02).to(torch.bfloat16)
+    q = quantize_int4_groupwise(w, g)
+    del w
+    sh = shard_groupwise(q, world, rank)
+    local = Groupwise4(sh.data.clone(), sh.scales.clone(), sh.shape, g)
+    cols = torch.arange(0, n, 1021, device=dev)
+    wcols = deq(q.data.view(n, k // 2)[cols].cpu().numpy().reshape(-1), q.scales[cols].cpu().numpy(),
+                (len(cols), k), g)
+    wround = {torch.bfloat16: torch.from_numpy(round_to_dtype(wcols, "bf16")).to(dev).double(),
+              torch.float16: torch.from_numpy(round_to_dtype(wcols, "f16")).to(dev).double()}
+    stream = torch.cuda.Stream(device=dev)
+    torch.cuda.synchronize()
+    layers = {mode: ShardedInt4Linear(local, n, mode=mode) for mode in ("p2p", "nccl")}
+    a, b = shard_bounds(n, world, rank)
+    cases, checks, launches, rel_worst, abs_worst = {}, {}, 0, 0.0, 0.0
+
+    def check(y, x, tag):
+        nonlocal rel_worst, abs_worst
+        ref = x.double() @ wround[x.dtype].T
+        err = y[:, cols].double() - ref
+        rel = (err.norm() / ref.norm()).item()
+        mab = err.abs().max().item()
+        assert rel <= 1e-3 and mab <= 2e-2, (tag, rel, mab)
+        rel_worst, abs_worst = max(rel_worst, rel), max(abs_worst, mab)
+
+    def one_gpu_ms(x, steps):
+        y1 = torch.empty(x.shape[0], n, device=dev)
+        call = lambda: int4_linear(x, q.data, q.scales, n, g, out=y1)  # noqa: E731
+        with torch.cuda.stream(stream):
+            for _ in range(2):
+                call()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                for _ in range(steps):
+                    call()
+            upload_graph(graph, stream)
+        torch.cuda.synchronize()
+        ms = _device_timed(stream, graph.replay, steps)
+        del graph
+        check(y1, x, "1gpu")
+        return _max_over_ranks(ms, dev, world)
+
+    def p2p_ms(x, steps, out_dtype):
+        lin = layers["p2p"]
+        with torch.cuda.stream(stream):
+            for _ in range(4):
+                y = lin(x, out_dtype=out_dtype)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                for _ in range(steps):  # an even count: the two output buffers alternate across replays
+                    y = lin(x, out_dtype=out_dtype)
+            upload_graph(graph, stream)
+        torch.cuda.synchronize()
+        dist.barrier()
+        torch.cuda.synchronize()
+        ms = _device_timed(stream, graph.replay, steps)
+        del graph
+        return _max_over_ranks(ms, dev, world), y
+
+    def nccl_ms(x, steps):
+        lin = layers["nccl"]
+        with torch.cuda.stream(stream):
+            for _ in range(2):
+                y = lin(x)
+        torch.cuda.synchronize()
+        dist.barrier()
+        torch.cuda.synchronize()
+        last = {}
+
+        def body():
+            for _ in range(steps):
+                last["y"] = lin(x)
+
+        ms = _device_timed(stream, body, steps, host_us_per_step=200.0)
+        y = last.pop("y")
+        slice_ = torch.empty(x.shape[0], -(-n // world), device=dev)
+        flat = torch.empty(world * x.shape[0], slice_.shape[1], device=dev)
+        with torch.cuda.stream(stream):
+            dist.all_gather_into_tensor(flat, slice_)
+        torch.cuda.synchronize()
+        dist.barrier()
+        torch.cuda.synchronize()
+
+        def gather():
+            for _ in range(steps):
+                dist.all_gather_into_tensor(flat, slice_)
+
+        g_ms = _device_timed(stream, gather, steps, host_us_per_step=100.0)
+        return _max_over_ranks(ms, dev, world), _max_over_ranks(g_ms, dev, world), y
+
+    for m in prefill_ms + decode_ms:
+        prefill = m >= 64
+        xdt = torch.bfloat16 if prefill else torch.float16
+        x = torch.randn(m, k, generator=torch.Generator(device=dev).manual_seed(600 + m), device=dev).to(xdt)
+        steps = (10 if m <= 2048 else 4) if prefill else 200
+        flops = 2.0 * m * n * k
+        t1 = one_gpu_ms(x, steps)
+        launches += steps + 2
+        kind = "prefill" if prefill else "decode"
+
+        def entry(ms):
+            e = {"ms": ms, "us": ms * 1e3, "efficiency_vs_1gpu": t1 / (world * ms), "one_gpu_ms": t1}
+            if prefill:
+                e["tflops"] = flops / (ms / 1e3) / 1e12
+                e["per_gpu_frac_of_peak"] = e["tflops"] / world / peaks["bf16_tflops"]
+            return e
+
+        ms, y = p2p_ms(x, steps, torch.float32)
+        check(y, x, f"p2p m{m}")
+        y32 = y[:, cols].clone()
+        cases[f"{kind}_m{m}_p2p_f32"] = entry(ms)
+        launches += 2 * (steps + 4)
+        if prefill:
+            ms, yb = p2p_ms(x, steps, torch.bfloat16)
+            assert torch.equal(yb[:, cols], y32.bfloat16()), f"bf16 output m{m}"
+            cases[f"{kind}_m{m}_p2p_bf16"] = entry(ms)
+            launches += 2 * (steps + 4)
+        if m in (2048, 1, 16):
+            ms, g_ms, y = nccl_ms(x, min(steps, 50))
+            check(y, x, f"nccl m{m}")
+            e = entry(ms)
+            e["allgather_ms"] = g_ms
+            cases[f"{kind}_m{m}_nccl_f32"] = e
+            launches += min(steps, 50) + 2
+        del x, y
+    for lin in layers.values():
+        lin.close()
+    del layers
+    torch.cuda.empty_cache()
+    head = cases.get("prefill_m2048_p2p_f32")
     return {
-        "metric": "INT4 dequant-GEMM TFLOP/s at M=2048, N-sharded + NCCL all-gather",
-        "workload": f"int4_gemm_m2048_k8192_n28672_g128_bf16_sharded{world}",
-        "value": tflops,
+        "metric": "N-column-sharded INT4 linear layer (Llama-3-70B gate/up, 8192->28672, g=128): whole-layer "
+                  "TFLOP/s at M=2048, fused p2p output",
+        "workload": f"int4_linear_sharded{world}_k8192_n28672_g128",
+        "value": head["tflops"] if head else None,
         "unit": "TFLOP/s",
-        "ms_per_step": ms,
-        "steps": steps,
         "scaling": "strong",
-        "allgather_bytes_per_step": m * n * 4,
-        "per_gpu_frac_of_peak": tflops / world / peaks["bf16_tflops"],
+        "n_gpus": world,
+        "shard_rows": [a, b],
+        "by_case": cases,
+        "modes": {"p2p": "kernels store each output element into every GPU's y over NVLink, then a bounded "
+                         "flag barrier (oq_int4_linear_peers + oq_peer_barrier)",
+                  "nccl": "local slice, NCCL all_gather_into_tensor, relayout copy"},
+        "output_bytes_per_gpu_per_call": {"m2048_f32": 2048 * n * 4 * (world - 1) // world},
+        "gpu_launches": launches,
+        "check": "every case: sampled columns over all shards vs the oracle's exactly-rounded weights "
+                 "(rel-L2 <= 1e-3, max-abs <= 2e-2); bf16 output == fp32 output rounded once",
+        "check_rel_l2": rel_worst,
+        "check_max_abs": abs_worst,
     }
 
 
@@ -871,31 +1174,11 @@ def run_ours(args):
         for i in range(COPIES)
     ]
 
-    def launch_many(count, h):
-        for i in range(count):
+    def launch_many(count, h, first=0):
+        for i in range(first, first + count):
             st = lib.oq_int4_linear(*args_c[i % COPIES], h)
             if st != 0:
                 raise RuntimeError(nat.last_error())
-
-    chunk = min(1024, max(1, args.steps))
-
-    def make_graph(count):
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.stream(stream):
-            launch_many(min(count, 8), ctypes.c_void_p(stream.cuda_stream))  # eager warm-up
-        stream.synchronize()
-        with torch.cuda.graph(g, stream=stream):
-            launch_many(count, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
-        return g
-
-    g_chunk = make_graph(chunk)
-    g_rest = make_graph(args.steps % chunk) if args.steps % chunk else None
-
-    # warm-up
-    wr = max(1, -(-args.warmup // chunk))
-    for _ in range(wr):
-        g_chunk.replay()
-    torch.cuda.synchronize()
 
     uuid = None
     try:
@@ -903,17 +1186,64 @@ def run_ours(args):
     except Exception:
         pass
     clocks = ClockSampler(uuid)
+
+    def make_graph(first, count):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            launch_many(count, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream), first=first)
+        upload_graph(g, stream)
+        return g
+
+    # Warm-up, exactly W launches: the first (up to 8) eagerly -- the kernels'
+    # first-launch set-up happens there, before any capture -- the rest as a
+    # graph replayed right before the timed launches.
+    eager = min(args.warmup, 8)
+    with torch.cuda.stream(stream):
+        launch_many(eager, ctypes.c_void_p(stream.cuda_stream))
+    stream.synchronize()
+    chunk = 1024
+    rest_w = args.warmup - eager
+    if rest_w + args.steps <= ONE_GRAPH_MAX:
+        graphs = {"warm": make_graph(eager, rest_w) if rest_w else None,
+                  "timed": make_graph(args.warmup, args.steps)}
+
+        def warm():
+            if graphs["warm"] is not None:
+                graphs["warm"].replay()
+
+        def timed():
+            graphs["timed"].replay()
+    else:
+        graphs = {c: make_graph(0, c) for c in {chunk, args.steps % chunk, rest_w % chunk} if c}
+
+        def replay(count):
+            """`count` launches: whole chunk graphs, then one graph of the rest."""
+            for _ in range(count // chunk):
+                graphs[chunk].replay()
+            if count % chunk:
+                graphs[count % chunk].replay()
+
+        def warm():
+            replay(rest_w)
+
+        def timed():
+            replay(args.steps)
+
+    torch.cuda.synchronize()
     clocks.start()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
+        # A device-side sleep first: the host submits the warm-up and timed
+        # graphs while the GPU sleeps, so the GPU runs the W warm-up launches
+        # and then the K timed ones back to back, and the events bracket the
+        # timed launches themselves, not the host's submission latency.
+        torch.cuda._sleep(int(2e6))
+        warm()
         start.record(stream)
-        for _ in range(args.steps // chunk):
-            g_chunk.replay()
-        if g_rest is not None:
-            g_rest.replay()
+        timed()
         end.record(stream)
     torch.cuda.synchronize()
     if world > 1:
@@ -932,7 +1262,8 @@ def run_ours(args):
     yref = x.double() @ wref.T
     y0 = int4_linear(x, packs[0], scs[0], N, G)
     rel = ((y0.double() - yref).norm() / yref.norm()).item()
-    assert rel < 1e-3, rel
+    mab = (y0.double() - yref).abs().max().item()
+    assert rel <= 1e-3 and mab <= 2e-2, (rel, mab)
 
     # e2e through the public API with host buffers.
     e2e_steps = min(args.steps, 2000)
@@ -969,23 +1300,14 @@ def run_ours(args):
         "unit": UNIT,
         "n_gpus": world,
         "steps": args.steps,
-        "warmup": wr * chunk,
+        "warmup": args.warmup,
         "ms_per_step": ms / args.steps,
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": "f16",
         "data": "synthetic",
-        "config": {
-            "workload": WORKLOAD,
-            "m": M, "k": K, "n": N, "group_size": G,
-            "weights": f"{COPIES} distinct INT4 copies rotated ({COPIES * ALG_BYTES / 1e6:.0f} MB > L2)",
-            "l2": "inputs larger than L2 (weight-copy rotation), no flush",
-            "launch": "CUDA graph of back-to-back launches (programmatic dependent launch)",
-            "static_weights": "weights quantized at setup and synchronized, so each launch streams them "
-                              "while the previous one drains (OQ_CONFIG_STATIC_WEIGHTS); x and y stay ordered",
-            "parallelism": f"dp{world} (each rank streams its own weight copies)",
-        },
+        "config": headline_config(world),
         "roofline": {
             "bound": "hbm",
             "achieved": achieved,
@@ -1007,22 +1329,25 @@ def run_ours(args):
         "gpu_launches": args.steps,
         "clocks": clk,
         "check_rel_l2": rel,
+        "check_max_abs": mab,
     }
     if not args.no_gemm:
         sys.path.insert(0, os.path.join(ROOT, "oracle"))
         if world == 1:
             line["also"] = [measure_gemm(dev, peaks), measure_w8a8(dev, peaks)]
         else:
-            line["also"] = [measure_sharded_gemm(dev, world, rank, peaks)]
+            line["also"] = [measure_sharded(dev, world, rank, peaks)]
     if world == 1 and not args.no_layers:
         line.setdefault("also", []).append(measure_decode_layers(dev, peaks))
         if not args.no_gemm:
             line["also"].append(measure_prefill_set(dev, peaks))
+        line["also"].append(measure_cpu_path_1024(dev, peaks))
     if not args.no_bulk:
         line.setdefault("also", []).append(measure_bulk_quant(dev, world, rank, peaks, layers=args.bulk_layers))
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline()
-    del g_chunk, g_rest
+    del graphs
+    line["summary"] = summarize(line)  # last key: the compact figures of every line
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

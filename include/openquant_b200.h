@@ -10,7 +10,8 @@
  *   - enqueues its kernels on the caller's CUDA stream (`stream`, a
  *     cudaStream_t passed as void*; NULL = the legacy default stream) and
  *     returns without synchronising;
- *   - allocates no device memory;
+ *   - allocates no device memory (oq_peer_alloc excepted: allocating is
+ *     its job);
  *   - returns OQ_OK (0) or an error code; oq_last_error() then returns a
  *     thread-local, NUL-terminated message.
  *
@@ -103,8 +104,9 @@ OQ_API int oq_device_count(void);
  * Synchronises the current device, then reads and clears the device-side
  * error word of the library's pipelined kernels: *code = 0 when none, 1 when
  * a kernel gave up waiting on one of its internal pipeline barriers (it then
- * returned early, its outputs are undefined).  No reference counterpart:
- * the reference's Triton kernel has no internal waits.
+ * returned early, its outputs are undefined), 2 when oq_peer_barrier gave
+ * up waiting for a peer GPU.  No reference counterpart: the reference's
+ * Triton kernel has no internal waits.
  */
 OQ_API int oq_take_device_error(int32_t *code);
 
@@ -217,6 +219,64 @@ OQ_API int oq_int4_linear_ex(const void *x, int x_dtype, const uint8_t *packed,
                              const float *bias, int64_t m, int64_t n, int64_t k,
                              int group_size, int kernel, int config,
                              oq_stream_t stream);
+
+/*
+ * N-column-sharded fused linear layer, one process per GPU: this GPU holds
+ * rows [col0, col0 + n) of the full layer's weights (a contiguous block of
+ * the groupwise layout: rows of packed and of scales) and computes
+ * y[:, col0:col0+n] of the full y[M][ld], and its kernels store every element
+ * of that slice into the y buffers of all n_gpus GPUs of the layer --
+ * y_gpus[0] this GPU's, y_gpus[1..] the peers' (mapped with oq_peer_import)
+ * -- at y_gpus[i][b * ld + col0 + f], with plain stores over NVLink.  That
+ * replaces the reference's fp32 (M, N) output allocation
+ * (openquant/triton_int4.py:120-122) with each GPU's share of the gathered
+ * output; the compute is oq_int4_linear_ex's (same kernels, same result per
+ * element), y_dtype / bias as there (bias: this shard's n features).
+ * Follow it with oq_peer_barrier on the same stream before reading y.
+ * n_gpus <= 8.  No counterpart in the reference (single-GPU only,
+ * openquant/fused_benchmark.py:53-54).
+ */
+OQ_API int oq_int4_linear_peers(const void *x, int x_dtype, const uint8_t *packed,
+                                const float *scales, void *const *y_gpus,
+                                int n_gpus, int y_dtype, const float *bias,
+                                int64_t ld, int64_t col0, int64_t m, int64_t n,
+                                int64_t k, int group_size, int kernel,
+                                int config, oq_stream_t stream);
+
+/* Bytes of the handle that oq_peer_export writes (a CUDA IPC handle). */
+#define OQ_PEER_HANDLE_BYTES 64
+
+/* Peer-mappable device memory for the sharded layer's outputs and flags:
+ * oq_peer_alloc allocates `bytes` on the current device, zeroed (it
+ * synchronises the device); oq_peer_free releases it (after every peer has
+ * closed its mapping).  oq_peer_export writes the buffer's handle
+ * (OQ_PEER_HANDLE_BYTES) for the other processes; oq_peer_import maps a
+ * peer's buffer into this process on the current device and oq_peer_close
+ * unmaps it.  No counterpart in the reference. */
+OQ_API int oq_peer_alloc(size_t bytes, void **ptr);
+OQ_API int oq_peer_free(void *ptr);
+OQ_API int oq_peer_export(const void *ptr, uint8_t *handle);
+OQ_API int oq_peer_import(const uint8_t *handle, void **ptr);
+OQ_API int oq_peer_close(void *ptr);
+
+/* Words of a flag array of oq_peer_barrier (uint32). */
+#define OQ_PEER_FLAG_WORDS 16
+
+/* Flag barrier of the sharded layer, enqueued on `stream` after the
+ * oq_int4_linear_peers call: flags_gpus[j] is GPU j's flag array of
+ * OQ_PEER_FLAG_WORDS uint32 (zeroed by oq_peer_alloc; flags_gpus[rank] this
+ * GPU's own).  After every kernel enqueued before it has finished, it counts
+ * itself (epoch = 1, 2, ...: this GPU's barrier count, kept in the last word
+ * of its own array, so a captured CUDA graph replays correctly), publishes
+ * the earlier kernels' writes (system-scope fence) and writes `epoch` into
+ * word `rank` of every GPU's array, then waits until words 0..world-1 of its
+ * own array hold `epoch` or later (wrap-around compare) -- all peers have
+ * finished storing into this GPU's y.  Every GPU of the layer calls it the
+ * same number of times.  The wait gives up after timeout_ns (0: 5 s), sets
+ * device error code 2 (oq_take_device_error) and returns.  No counterpart in
+ * the reference. */
+OQ_API int oq_peer_barrier(uint32_t *const *flags_gpus, int world, int rank,
+                           int64_t timeout_ns, oq_stream_t stream);
 
 /* W8A8 linear layer on the tcgen05 tensor cores (kind::i8, int32 sums):
  * y[m][n] = sx[m] * sw[n] * sum_k qx[m][k] * qw[n][k].  qx / sx and qw / sw

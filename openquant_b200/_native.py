@@ -38,7 +38,17 @@ SIGNATURES = {
     "oq_int8_gemm": (_I32, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _P]),
     "oq_int4_linear_ex": (_I32, [_P, _I32, _P, _P, _P, _I32, _P, _I64, _I64, _I64, _I32, _I32, _I32, _P]),
     "oq_int8_linear_noalloc": (_I32, [_P, _I32, _P, _P, _P, _I64, _I64, _I64, _P]),
+    "oq_int4_linear_peers": (_I32, [_P, _I32, _P, _P, _P, _I32, _I32, _P, _I64, _I64, _I64, _I64, _I64, _I32, _I32,
+                                    _I32, _P]),
+    "oq_peer_alloc": (_I32, [ctypes.c_size_t, _P]),
+    "oq_peer_free": (_I32, [_P]),
+    "oq_peer_export": (_I32, [_P, _P]),
+    "oq_peer_import": (_I32, [_P, _P]),
+    "oq_peer_close": (_I32, [_P]),
+    "oq_peer_barrier": (_I32, [_P, _I32, _I32, _I64, _P]),
 }
+PEER_HANDLE_BYTES = 64
+PEER_FLAG_WORDS = 16
 
 _lock = threading.Lock()
 _lib = None

@@ -53,25 +53,90 @@ inline int dtype_size(int dtype) {
     }
 }
 
-// Number of SMs of the current device (cached per device).
+// Most GPUs one sharded output is written to (this one and its peers).
+constexpr int kMaxOutGpus = 8;
+
 // Output of a linear layer: y[b][feature] as fp32, fp16 or bf16 (OQ_F32 /
 // OQ_F16 / OQ_BF16), with an optional fp32 bias per output feature added in
-// fp32 before the single rounding to the output type.
+// fp32 before the single rounding to the output type.  Element (b, f) goes
+// to y[b * ld + col0 + f] -- ld = the layer's N and col0 = 0 for a plain
+// layer; for an N-column shard, ld is the full layer's N and col0 the
+// shard's first column -- and, for a shard, to the same element of each
+// peer GPU's output (npeers buffers mapped over NVLink, plain stores).
 struct OutSpec {
     void *y;
     const float *bias;  // nullptr: no bias
     int dtype;
-    __device__ __forceinline__ void store(size_t idx, int feature, float v) const {
+    int npeers = 0;
+    int64_t ld = 0;
+    int64_t col0 = 0;
+    void *peer[kMaxOutGpus - 1] = {};
+
+    template <typename T>
+    __device__ __forceinline__ void put(T v, size_t idx) const {
+        static_cast<T *>(y)[idx] = v;
+#pragma unroll
+        for (int p = 0; p < kMaxOutGpus - 1; ++p)  // constant indices: the pointers stay in the parameter bank
+            if (p < npeers) static_cast<T *>(peer[p])[idx] = v;
+    }
+    __device__ __forceinline__ void store(int64_t b, int feature, float v) const {
         if (bias != nullptr) v += __ldg(bias + feature);
+        const size_t idx = (size_t)(b * ld + col0 + feature);
         if (dtype == OQ_F16)
-            static_cast<__half *>(y)[idx] = __float2half_rn(v);
+            put(__float2half_rn(v), idx);
         else if (dtype == OQ_BF16)
-            static_cast<__nv_bfloat16 *>(y)[idx] = __float2bfloat16_rn(v);
+            put(__float2bfloat16_rn(v), idx);
         else
-            static_cast<float *>(y)[idx] = v;
+            put(v, idx);
+    }
+    // Stores v[j] (fp32 bit patterns) as batch rows b0 + j < bend of one
+    // feature: a GEMM epilogue's column of the accumulator.  Converts once,
+    // then writes the run to each destination in turn (one GPU's stores
+    // back to back).
+    template <int CNT>
+    __device__ __forceinline__ void store_run(int64_t b0, int64_t bend, int feature, const uint32_t (&v)[CNT]) const {
+        const int64_t off = b0 * ld + col0 + feature;
+        const int64_t cnt = bend - b0;
+        float bv = 0.0f;
+        if (bias != nullptr) bv = __ldg(bias + feature);
+        if (dtype == OQ_F16)
+            put_run<__half>(off, cnt, v, bv);
+        else if (dtype == OQ_BF16)
+            put_run<__nv_bfloat16>(off, cnt, v, bv);
+        else
+            put_run<float>(off, cnt, v, bv);
+    }
+    template <typename T, int CNT>
+    __device__ __forceinline__ void put_run(int64_t off, int64_t cnt, const uint32_t (&v)[CNT], float bv) const {
+        T vals[CNT];
+#pragma unroll
+        for (int j = 0; j < CNT; ++j) {
+            float f = __uint_as_float(v[j]);
+            if (bias != nullptr) f += bv;  // no bias: no add (it would turn -0 into +0)
+            if constexpr (std::is_same<T, __half>::value)
+                vals[j] = __float2half_rn(f);
+            else if constexpr (std::is_same<T, __nv_bfloat16>::value)
+                vals[j] = __float2bfloat16_rn(f);
+            else
+                vals[j] = f;
+        }
+#pragma unroll
+        for (int d = 0; d < kMaxOutGpus; ++d) {
+            if (d > npeers) break;
+            T *dst = static_cast<T *>(d == 0 ? y : peer[d > 0 ? d - 1 : 0]) + off;
+            if (cnt >= CNT) {
+#pragma unroll
+                for (int j = 0; j < CNT; ++j) dst[j * ld] = vals[j];
+            } else {
+#pragma unroll
+                for (int j = 0; j < CNT; ++j)
+                    if (j < cnt) dst[j * ld] = vals[j];
+            }
+        }
     }
 };
 
+// Number of SMs of the current device (cached per device).
 int sm_count();
 // Raises a kernel's dynamic shared-memory limit to `bytes` on the current
 // device (once per kernel, device and size; thread-safe).

@@ -233,13 +233,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 uint32_t v[32];
                 tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + c * 32, v);
                 tc_wait_ld();
-                if (row < n) {
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const int mb = m0 + c * 32 + j;
-                        if (mb < m) y.store((size_t)mb * n + row, row, __uint_as_float(v[j]));
-                    }
-                }
+                if (row < n) y.store_run(m0 + c * 32, m, row, v);
             }
             tc_fence_before();
             __syncwarp();
@@ -443,13 +437,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 uint32_t v[32];
                 tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + c * 32, v);
                 tc_wait_ld();
-                if (row < n) {
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const int mb = m0 + c * 32 + j;
-                        if (mb < m) y.store((size_t)mb * n + row, row, __uint_as_float(v[j]));
-                    }
-                }
+                if (row < n) y.store_run(m0 + c * 32, m, row, v);
             }
             tc_fence_before();
             __syncwarp();

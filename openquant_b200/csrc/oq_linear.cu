@@ -434,7 +434,7 @@ __global__ void __launch_bounds__(WARPS * 32, MINB) gemv_int4_kernel(const XT *_
                         const int g2 = ln >> 2, t2 = ln & 3;
                         const int row = row0 + g2 + (e >= 2 ? 8 : 0);
                         const int mb = 8 * j + 2 * t2 + (e & 1);
-                        if (row < n && mb < m) y.store((size_t)mb * n + row, row, v);
+                        if (row < n && mb < m) y.store(mb, row, v);
                     }
                     jj = 0;
                     ++ti;
@@ -672,12 +672,12 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW <= 8 ? 2 : 1)
                 const int row = row0 + g2 + (e >= 2 ? 8 : 0);
                 const int mb = 8 * j + 2 * t2 + (e & 1);
                 if (gate_n == 0) {
-                    if (ok && row < n && mb < m) y.store((size_t)mb * n + row, row, v);
+                    if (ok && row < n && mb < m) y.store(mb, row, v);
                 } else if ((ti & 1) == 0) {
                     gsave = v;  // gate tile: kept until the matching up tile
                 } else {
                     const int f = row - gate_n;  // output feature
-                    if (ok && f < gate_n && mb < m) y.store((size_t)mb * gate_n + f, f, gsave / (1.0f + expf(-gsave)) * v);
+                    if (ok && f < gate_n && mb < m) y.store(mb, f, gsave / (1.0f + expf(-gsave)) * v);
                 }
             }
             // One reduction slot: every read of it ends before the next
@@ -838,7 +838,7 @@ __global__ void __launch_bounds__(256, 4)
         const int g2 = ln >> 2, t2 = ln & 3;
         const int row = row0 + g2 + (e >= 2 ? 8 : 0);
         const int mb = 8 * j + 2 * t2 + (e & 1);
-        if (ok && row < n && mb < m) y.store((size_t)mb * n + row, row, v);
+        if (ok && row < n && mb < m) y.store(mb, row, v);
     }
 }
 
@@ -1002,7 +1002,7 @@ __global__ void __launch_bounds__(512, 2)
         const int g2 = ln >> 2, t2 = ln & 3;
         const int row = row0 + g2 + (e >= 2 ? 8 : 0);
         const int mb = 8 * j + 2 * t2 + (e & 1);
-        if (ok && row < n && mb < m) y.store((size_t)mb * n + row, row, v);
+        if (ok && row < n && mb < m) y.store(mb, row, v);
     }
 }
 
@@ -1033,7 +1033,7 @@ __global__ void __launch_bounds__(256) simt_int4_kernel(const XT *__restrict__ x
                 float v = acc[i];
 #pragma unroll
                 for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-                if (lane == 0 && m0 + i < m) y.store((size_t)(m0 + i) * n + row, (int)row, v);
+                if (lane == 0 && m0 + i < m) y.store(m0 + i, (int)row, v);
             }
         }
     }
@@ -1519,6 +1519,8 @@ int int4_linear_impl(const void *x, int x_dtype, const uint8_t *packed, const fl
     OQ_REQUIRE(m >= 1 && n >= 1 && k >= 1, "Matrix dimensions must be positive");
     OQ_REQUIRE(x && packed && scales && y.y, "null pointer argument");
     OQ_REQUIRE(y.dtype == OQ_F32 || y.dtype == OQ_F16 || y.dtype == OQ_BF16, "output dtype must be fp32, fp16 or bf16");
+    if (y.ld == 0) y.ld = n;
+    OQ_REQUIRE(y.col0 >= 0 && y.col0 + n <= y.ld, "output columns [col0, col0 + n) must lie in a row of ld");
     const int64_t kp = cdiv(k, group_size) * group_size;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (config & OQ_CONFIG_SILU_GATE) {
@@ -1581,4 +1583,23 @@ extern "C" int oq_int4_linear_ex(const void *x, int x_dtype, const uint8_t *pack
     clear_error();
     return int4_linear_impl(x, x_dtype, packed, scales, OutSpec{y, bias, y_dtype}, m, n, k, group_size, kernel,
                             config, stream);
+}
+
+extern "C" int oq_int4_linear_peers(const void *x, int x_dtype, const uint8_t *packed, const float *scales,
+                                    void *const *y_gpus, int n_gpus, int y_dtype, const float *bias, int64_t ld,
+                                    int64_t col0, int64_t m, int64_t n, int64_t k, int group_size, int kernel,
+                                    int config, oq_stream_t stream) {
+    clear_error();
+    OQ_REQUIRE(y_gpus != nullptr && n_gpus >= 1 && n_gpus <= kMaxOutGpus, "n_gpus must be in [1, %d]", kMaxOutGpus);
+    OQ_REQUIRE(ld >= 1 && col0 >= 0 && col0 + n <= ld, "output columns [col0, col0 + n) must lie in a row of ld");
+    OQ_REQUIRE(m < (1ll << 40) / ld, "output too large");
+    OutSpec out{y_gpus[0], bias, y_dtype};
+    out.npeers = n_gpus - 1;
+    out.ld = ld;
+    out.col0 = col0;
+    for (int i = 1; i < n_gpus; ++i) {
+        OQ_REQUIRE(y_gpus[i] != nullptr, "null output pointer for GPU %d", i);
+        out.peer[i - 1] = y_gpus[i];
+    }
+    return int4_linear_impl(x, x_dtype, packed, scales, out, m, n, k, group_size, kernel, config, stream);
 }
