@@ -220,6 +220,30 @@ OQ_API int oq_int4_linear_ex(const void *x, int x_dtype, const uint8_t *packed,
                              int group_size, int kernel, int config,
                              oq_stream_t stream);
 
+/* oq_int4_linear_ex with a caller workspace for the tcgen05 GEMM: when the
+ * tiles do not divide evenly over the SMs, the GEMM splits the work evenly
+ * (stream-K: some tiles computed in pieces by two or more SMs), keeps the
+ * pieces' fp32 sums in `workspace` (device, 16-byte aligned, contents
+ * ignored) and adds them in k order in a second kernel on the stream -- a
+ * fixed order, so the result is deterministic; it differs from the unsplit
+ * kernel's only in fp32 summation order.  ws_bytes below
+ * oq_int4_linear_workspace_bytes(...) (or workspace NULL) runs the unsplit
+ * kernel.  The workspace is in use until the call's work on `stream` ends.
+ * The same computation as int4_linear, openquant/triton_int4.py:78-138
+ * (same output contract, :120-122). */
+OQ_API int oq_int4_linear_ws(const void *x, int x_dtype, const uint8_t *packed,
+                             const float *scales, void *y, int y_dtype,
+                             const float *bias, int64_t m, int64_t n, int64_t k,
+                             int group_size, int kernel, int config,
+                             void *workspace, size_t ws_bytes,
+                             oq_stream_t stream);
+
+/* Workspace bytes oq_int4_linear_ws uses for this shape and kernel choice
+ * (0: the chosen kernel takes none).  Never fails (0 for invalid shapes). */
+OQ_API int64_t oq_int4_linear_workspace_bytes(int64_t m, int64_t n, int64_t k,
+                                              int group_size, int kernel,
+                                              int config);
+
 /*
  * N-column-sharded fused linear layer, one process per GPU: this GPU holds
  * rows [col0, col0 + n) of the full layer's weights (a contiguous block of
@@ -232,8 +256,9 @@ OQ_API int oq_int4_linear_ex(const void *x, int x_dtype, const uint8_t *packed,
  * (openquant/triton_int4.py:120-122) with each GPU's share of the gathered
  * output; the compute is oq_int4_linear_ex's (same kernels, same result per
  * element), y_dtype / bias as there (bias: this shard's n features).
- * Follow it with oq_peer_barrier on the same stream before reading y.
- * n_gpus <= 8.  No counterpart in the reference (single-GPU only,
+ * workspace / ws_bytes as oq_int4_linear_ws.  Follow it with
+ * oq_peer_barrier on the same stream before reading y.  n_gpus <= 8.  No
+ * counterpart in the reference (single-GPU only,
  * openquant/fused_benchmark.py:53-54).
  */
 OQ_API int oq_int4_linear_peers(const void *x, int x_dtype, const uint8_t *packed,
@@ -241,7 +266,8 @@ OQ_API int oq_int4_linear_peers(const void *x, int x_dtype, const uint8_t *packe
                                 int n_gpus, int y_dtype, const float *bias,
                                 int64_t ld, int64_t col0, int64_t m, int64_t n,
                                 int64_t k, int group_size, int kernel,
-                                int config, oq_stream_t stream);
+                                int config, void *workspace, size_t ws_bytes,
+                                oq_stream_t stream);
 
 /* Bytes of the handle that oq_peer_export writes (a CUDA IPC handle). */
 #define OQ_PEER_HANDLE_BYTES 64

@@ -39,7 +39,10 @@ SIGNATURES = {
     "oq_int4_linear_ex": (_I32, [_P, _I32, _P, _P, _P, _I32, _P, _I64, _I64, _I64, _I32, _I32, _I32, _P]),
     "oq_int8_linear_noalloc": (_I32, [_P, _I32, _P, _P, _P, _I64, _I64, _I64, _P]),
     "oq_int4_linear_peers": (_I32, [_P, _I32, _P, _P, _P, _I32, _I32, _P, _I64, _I64, _I64, _I64, _I64, _I32, _I32,
-                                    _I32, _P]),
+                                    _I32, _P, ctypes.c_size_t, _P]),
+    "oq_int4_linear_ws": (_I32, [_P, _I32, _P, _P, _P, _I32, _P, _I64, _I64, _I64, _I32, _I32, _I32, _P,
+                                 ctypes.c_size_t, _P]),
+    "oq_int4_linear_workspace_bytes": (_I64, [_I64, _I64, _I64, _I32, _I32, _I32]),
     "oq_peer_alloc": (_I32, [ctypes.c_size_t, _P]),
     "oq_peer_free": (_I32, [_P]),
     "oq_peer_export": (_I32, [_P, _P]),

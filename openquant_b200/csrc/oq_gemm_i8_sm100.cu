@@ -33,6 +33,8 @@
 
 #include <algorithm>
 #include <mutex>
+#include <utility>
+#include <vector>
 
 namespace oq {
 namespace {
@@ -276,33 +278,59 @@ namespace {
 
 constexpr int64_t kNoAllocQxBytes = int64_t(16) << 20;  // int8 activations, M * K
 constexpr int64_t kNoAllocRows = 16384;                 // per-token fp32 scales
-constexpr int kNoAllocMaxDevices = 64;
 
 // [0, 16 MiB): qx [M][K] int8; [16 MiB, +64 KiB): sx [M] fp32.
 static __device__ __align__(256) uint8_t g_w8a8_scratch[kNoAllocQxBytes + kNoAllocRows * 4];
 
 std::mutex g_scratch_mutex;
-void *g_scratch_address[kNoAllocMaxDevices] = {};
+// Resolved addresses, one per CUDA context: a device can carry more than one
+// context (a primary one and ones made with cuCtxCreate), and the array has
+// a different address in each.
+std::vector<std::pair<CUcontext, void *>> g_scratch_address;
 
-// Device address of g_w8a8_scratch on the current device.  Host code only
+CUresult current_context(CUcontext *ctx) {
+    static PFN_cuCtxGetCurrent_v4000 get = nullptr;
+    if (get == nullptr) {
+        cudaDriverEntryPointQueryResult q;
+        void *fn = nullptr;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess || fn == nullptr)
+            return CUDA_ERROR_NOT_FOUND;
+        get = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(fn);
+    }
+    return get(ctx);
+}
+
+// Device address of g_w8a8_scratch in the current context.  Host code only
 // sees a host-side stand-in under that name, so the address is looked up
-// once per device (cudaGetSymbolAddress, with that device current) and kept.
+// once per context (cudaGetSymbolAddress, with that context current) and
+// kept.  A context destroyed and made again (cudaDeviceReset) can come back
+// under the same handle with the array elsewhere, which this cache cannot
+// tell: the entry point is not for processes that reset a device.
 int scratch_address(void **out) {
     int dev = -1;
     OQ_CUDA(cudaGetDevice(&dev));
-    if (dev < 0 || dev >= kNoAllocMaxDevices) return invalid("device ordinal %d out of range for the fixed scratch", dev);
-    std::lock_guard<std::mutex> lock(g_scratch_mutex);
-    if (g_scratch_address[dev] == nullptr) {
-        void *p = nullptr;
-        const cudaError_t err = cudaGetSymbolAddress(&p, g_w8a8_scratch);
-        if (err != cudaSuccess || p == nullptr) {
-            set_error("int8 linear (no-alloc): cannot resolve the scratch array on device %d: %s", dev,
-                      cudaGetErrorString(err));
-            return OQ_ERR_CUDA;
-        }
-        g_scratch_address[dev] = p;
+    OQ_CUDA(cudaSetDevice(dev));  // the same device: makes its primary context current if none is
+    CUcontext ctx = nullptr;
+    if (current_context(&ctx) != CUDA_SUCCESS || ctx == nullptr) {
+        set_error("int8 linear (no-alloc): no current CUDA context on device %d", dev);
+        return OQ_ERR_CUDA;
     }
-    *out = g_scratch_address[dev];
+    std::lock_guard<std::mutex> lock(g_scratch_mutex);
+    for (const auto &e : g_scratch_address)
+        if (e.first == ctx) {
+            *out = e.second;
+            return OQ_OK;
+        }
+    void *p = nullptr;
+    const cudaError_t err = cudaGetSymbolAddress(&p, g_w8a8_scratch);
+    if (err != cudaSuccess || p == nullptr) {
+        set_error("int8 linear (no-alloc): cannot resolve the scratch array on device %d: %s", dev,
+                  cudaGetErrorString(err));
+        return OQ_ERR_CUDA;
+    }
+    g_scratch_address.emplace_back(ctx, p);
+    *out = p;
     return OQ_OK;
 }
 

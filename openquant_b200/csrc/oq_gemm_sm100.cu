@@ -60,10 +60,113 @@ constexpr size_t kSmemBytes = 1024 + (size_t)kStages * (kXBytes + kWBytes) + 256
 
 static_assert(kAccCols + kStages * kACols <= kTmemCols, "TMEM budget");
 
+// The work of one CTA as a sequence of segments (tile, k-blocks [kb0, kb1)).
+// Tiles [0, t0) go whole, in rounds over the persistent grid: tiles
+// blockIdx.x, blockIdx.x + gridDim.x, ... (t0 a multiple of the grid, so
+// every CTA takes the same number of them, and the CTAs of a round work on
+// neighbouring tiles, which share weight tiles and x in L2).  The remaining
+// tiles [t0, tiles) -- the part of a last round that would leave SMs idle --
+// are split evenly (stream-K): their k-blocks laid end to end as units
+// u = (tile - t0) * kblocks + kb, CTA c taking [U c / G, U (c + 1) / G).
+// A tile cut by a CTA boundary is computed in pieces whose fp32 sums go to a
+// workspace and are added by streamk_fixup_kernel.  Only the first and last
+// segments of a CTA's split range can be pieces.  t0 == tiles: no split.
+struct Segments {
+    int tiles, kblocks, t0;
+    int tile;
+    int64_t u, u1;
+    __device__ Segments(int tiles_, int kblocks_, int t0_) : tiles(tiles_), kblocks(kblocks_), t0(t0_) {
+        const int64_t units = (int64_t)(tiles - t0) * kblocks;
+        tile = blockIdx.x;
+        u = units * blockIdx.x / gridDim.x;
+        u1 = units * (blockIdx.x + 1) / gridDim.x;
+    }
+    // `piece_index` counts the segments of the split range: 0 for the first.
+    __device__ bool next(int &t, int &kb0, int &kb1, int &piece_index) {
+        if (tile < t0) {
+            t = tile, kb0 = 0, kb1 = kblocks, piece_index = -1;
+            tile += gridDim.x;
+            return true;
+        }
+        if (u >= u1) return false;
+        t = t0 + (int)(u / kblocks);
+        kb0 = (int)(u % kblocks);
+        const int64_t left = u1 - u;
+        kb1 = left < (int64_t)(kblocks - kb0) ? kb0 + (int)left : kblocks;
+        piece_index = (tile == INT32_MAX) ? 1 : 0;
+        tile = INT32_MAX;  // marks: the split range has started
+        u += kb1 - kb0;
+        return true;
+    }
+};
+
+// Workspace slot of a piece: 2c for CTA c's first segment, 2c + 1 for its
+// last.  A slot holds the piece's fp32 sums as [bx / 32][32][128]: chunk c
+// of 32 batch rows, batch row j of the chunk, weight row r -- the epilogue's
+// thread r writes v[j] at [c][j][r], so each warp store is 128 coalesced bytes.
+__device__ __forceinline__ void store_piece(float *slot, int c, int r, const uint32_t (&v)[32]) {
+    float *dst = slot + (size_t)c * 32 * 128 + r;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) dst[j * 128] = __uint_as_float(v[j]);
+}
+
+// Adds the pieces of the split tiles, in k order, and writes them through
+// the OutSpec.  `first.c[i]` is the first CTA boundary inside split tile i
+// (the host lists them); blockIdx.x = i, and blockIdx.y picks the chunk
+// [blockIdx.y * per, (blockIdx.y + 1) * per) of the tile's elements
+// (gridDim.y chunks, sized so that the CTAs fill the GPU: a few split tiles
+// can have ~100 pieces each).
+constexpr int kMaxPiecesPerTile = 160;  // >= the grid (148 SMs) + 1
+
+struct FixupList {
+    int16_t c[kMaxPiecesPerTile];
+};
+
+__global__ void __launch_bounds__(256) streamk_fixup_kernel(const float *__restrict__ ws, OutSpec y, int m, int n,
+                                                          int tiles_m, int bx, int kblocks, int t0, int64_t units,
+                                                          int grid, FixupList first) {
+    __shared__ const float *src[kMaxPiecesPerTile];
+    __shared__ int npieces;
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int c = first.c[blockIdx.x];
+    auto u0 = [&](int cc) { return units * cc / grid; };
+    const int64_t t = u0(c) / kblocks;                    // split tile t0 + t
+    const size_t slot_floats = (size_t)bx * 128;
+    if (threadIdx.x == 0) {
+        // the CTAs holding the tile's pieces, in k order: c - 1 (the first), c, ...
+        int np = 0;
+        for (int cc = c - 1; cc < grid && (cc < c || u0(cc) < (t + 1) * kblocks) && np < kMaxPiecesPerTile; ++cc)
+            src[np++] = ws + (2 * (size_t)cc + (u0(cc) >= t * kblocks ? 0 : 1)) * slot_floats;
+        npieces = np;
+    }
+    __syncthreads();
+    const int np = npieces;
+    const int64_t tile = t0 + t;
+    const int n0 = (int)(tile / tiles_m) * 128, m0 = (int)(tile % tiles_m) * bx;
+    const int total = bx * 128, per = (total + (int)gridDim.y - 1) / (int)gridDim.y;
+    const int e1 = min(total, (int)(blockIdx.y + 1) * per);
+    for (int idx = (int)blockIdx.y * per + threadIdx.x; idx < e1; idx += blockDim.x) {
+        const int r = idx & 127, bj = idx >> 7;           // bj = 32 chunk + j
+        float v = src[0][idx];
+        // eight loads in flight, then the adds in k order
+        for (int i0 = 1; i0 < np; i0 += 8) {
+            float part[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) part[i] = i0 + i < np ? src[i0 + i][idx] : 0.0f;
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                if (i0 + i < np) v += part[i];
+        }
+        const int b = m0 + bj, f = n0 + r;
+        if (b < m && f < n) y.store(b, f, v);
+    }
+}
+
 template <typename XT>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_int4_tcgen05_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
-                             const float *__restrict__ scales, OutSpec y, int m, int n, int kp, int g) {
+                             const float *__restrict__ scales, OutSpec y, int m, int n, int kp, int g, int t0,
+                             float *__restrict__ ws) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
     uint8_t *xbuf = smem;                                    // [S][256 rows][128 B], swizzled
@@ -112,9 +215,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_prefetch_desc(&wmap);
             int it = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+            Segments seg(tiles, kblocks, t0);
+            int tile, kb0, kb1, pi;
+            while (ok && seg.next(tile, kb0, kb1, pi)) {
                 const int n0 = (tile / tiles_m) * kBN, m0 = (tile % tiles_m) * kBX;
-                for (int kb = 0; kb < kblocks; ++kb, ++it) {
+                for (int kb = kb0; kb < kb1; ++kb, ++it) {
                     const int s = it % kStages, r = it / kStages;
                     if (r > 0 && !(ok = mbar_wait(&empty[s], (r - 1) & 1))) break;
                     mbar_arrive_expect_tx(&full[s], kXBytes + kWBytes);
@@ -133,10 +238,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             constexpr uint32_t idesc = umma_idesc_f16(kBN, kBX, std::is_same<XT, __nv_bfloat16>::value);
             int it = 0, ti = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++ti) {
+            Segments seg(tiles, kblocks, t0);
+            int tile, kb0, kb1, pi;
+            for (; ok && seg.next(tile, kb0, kb1, pi); ++ti) {
                 if (ti > 0 && !(ok = mbar_wait(acc_empty, (ti - 1) & 1))) break;
                 tc_fence_after();
-                for (int kb = 0; kb < kblocks; ++kb, ++it) {
+                for (int kb = kb0; kb < kb1; ++kb, ++it) {
                     const int s = it % kStages, r = it / kStages;
                     if (!(ok = mbar_wait(&full[s], r & 1))) break;
                     if (!(ok = mbar_wait(&deq[s], r & 1))) break;
@@ -146,7 +253,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int kk = 0; kk < kBK / 16; ++kk)
                         tc_mma_ts(tmem, a_tmem + kk * 8, bdesc + (uint64_t)(kk * 32 / 16), idesc,
-                                  (kb | kk) != 0 ? 1u : 0u);
+                                  (kb != kb0 || kk != 0) ? 1u : 0u);
                     tc_commit(&empty[s]);
                 }
                 if (ok) tc_commit(acc_full);
@@ -163,10 +270,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int r = q * 32 + lane;    // weight row within the tile
         int it = 0;
         bool ok = true;
-        for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+        Segments seg(tiles, kblocks, t0);
+        int tile, kb0, kb1, pi;
+        while (ok && seg.next(tile, kb0, kb1, pi)) {
             const int n0 = (tile / tiles_m) * kBN;
             const float *srow = scales + (size_t)min(n0 + r, n - 1) * groups;
-            for (int kb = 0; kb < kblocks; ++kb, ++it) {
+            for (int kb = kb0; kb < kb1; ++kb, ++it) {
                 const int s = it % kStages, rd = it / kStages;
                 const int c0 = kb * kBK;
                 // words 0-3 of a row's k-block are columns c0..c0+31 (scale
@@ -222,18 +331,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int q = warp - 4;
         int ti = 0;
         bool ok = true;
-        for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++ti) {
+        Segments seg(tiles, kblocks, t0);
+        int tile, kb0, kb1, pi;
+        for (; ok && seg.next(tile, kb0, kb1, pi); ++ti) {
             const int n0 = (tile / tiles_m) * kBN, m0 = (tile % tiles_m) * kBX;
             ok = __all_sync(0xffffffffu, mbar_wait(acc_full, ti & 1));  // tcgen05.ld is .sync.aligned
             if (!ok) break;
             tc_fence_after();
             const int row = n0 + q * 32 + lane;
+            const bool piece = kb0 != 0 || kb1 != kblocks;
+            float *slot = ws + (2 * (size_t)blockIdx.x + (pi == 0 ? 0 : 1)) * (size_t)(kAccCols * kBN);
 #pragma unroll 1
             for (int c = 0; c < kAccCols / 32; ++c) {
                 uint32_t v[32];
                 tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + c * 32, v);
                 tc_wait_ld();
-                if (row < n) y.store_run(m0 + c * 32, m, row, v);
+                if (piece)
+                    store_piece(slot, c, q * 32 + lane, v);
+                else if (row < n)
+                    y.store_run(m0 + c * 32, m, row, v);
             }
             tc_fence_before();
             __syncwarp();
@@ -270,7 +386,8 @@ static_assert(kWideACol + 2 * kACols <= kTmemCols, "wide TMEM budget");
 template <typename XT>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_int4_tcgen05_wide_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
-                                  const float *__restrict__ scales, OutSpec y, int m, int n, int kp, int g, int nb) {
+                                  const float *__restrict__ scales, OutSpec y, int m, int n, int kp, int g, int nb,
+                                  int t0, float *__restrict__ ws) {
     static_assert(kDqSplit == 1, "the wide kernel keeps one dequant warp per TMEM lane quarter");
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
@@ -326,9 +443,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             int it = 0;
             bool ok = true;
             const uint32_t tx = (uint32_t)(bx * kBK * 2 + kWBytes);
-            for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+            Segments seg(tiles, kblocks, t0);
+            int tile, kb0, kb1, pi;
+            while (ok && seg.next(tile, kb0, kb1, pi)) {
                 const int n0 = (tile / tiles_m) * kBN, m0 = (tile % tiles_m) * bx;
-                for (int kb = 0; kb < kblocks; ++kb, ++it) {
+                for (int kb = kb0; kb < kb1; ++kb, ++it) {
                     const int s = it % kWideStages, r = it / kWideStages;
                     if (r > 0 && !(ok = mbar_wait(&empty[s], (r - 1) & 1))) break;
                     uint8_t *xs = xbuf + (size_t)s * kWideXBytes;
@@ -348,10 +467,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t idesc = umma_idesc_f16(kBN, nb, std::is_same<XT, __nv_bfloat16>::value);
             int it = 0, ti = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++ti) {
+            Segments seg(tiles, kblocks, t0);
+            int tile, kb0, kb1, pi;
+            for (; ok && seg.next(tile, kb0, kb1, pi); ++ti) {
                 if (ti > 0 && !(ok = mbar_wait(acc_empty, (ti - 1) & 1))) break;
                 tc_fence_after();
-                for (int kb = 0; kb < kblocks; ++kb, ++it) {
+                for (int kb = kb0; kb < kb1; ++kb, ++it) {
                     const int s = it % kWideStages, a = it & 1;
                     if (!(ok = mbar_wait(&full[s], (it / kWideStages) & 1))) break;
                     if (!(ok = mbar_wait(&deq[a], (it >> 1) & 1))) break;
@@ -361,7 +482,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t a_tmem = tmem + kWideACol + a * kACols;
 #pragma unroll
                     for (int kk = 0; kk < kBK / 16; ++kk) {
-                        const uint32_t acc = (kb | kk) != 0 ? 1u : 0u;
+                        const uint32_t acc = (kb != kb0 || kk != 0) ? 1u : 0u;
                         tc_mma_ts(tmem, a_tmem + kk * 8, b0 + (uint64_t)(kk * 32 / 16), idesc, acc);
                         tc_mma_ts(tmem + nb, a_tmem + kk * 8, b1 + (uint64_t)(kk * 32 / 16), idesc, acc);
                     }
@@ -380,10 +501,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int r = q * 32 + lane;    // weight row within the tile
         int it = 0;
         bool ok = true;
-        for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+        Segments seg(tiles, kblocks, t0);
+        int tile, kb0, kb1, pi;
+        while (ok && seg.next(tile, kb0, kb1, pi)) {
             const int n0 = (tile / tiles_m) * kBN;
             const float *srow = scales + (size_t)min(n0 + r, n - 1) * groups;
-            for (int kb = 0; kb < kblocks; ++kb, ++it) {
+            for (int kb = kb0; kb < kb1; ++kb, ++it) {
                 const int s = it % kWideStages, a = it & 1;
                 const int c0 = kb * kBK;
                 const float s0 = __ldg(srow + min(c0 / g, groups - 1));
@@ -426,18 +549,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int q = warp - 4;
         int ti = 0;
         bool ok = true;
-        for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++ti) {
+        Segments seg(tiles, kblocks, t0);
+        int tile, kb0, kb1, pi;
+        for (; ok && seg.next(tile, kb0, kb1, pi); ++ti) {
             const int n0 = (tile / tiles_m) * kBN, m0 = (tile % tiles_m) * bx;
             ok = __all_sync(0xffffffffu, mbar_wait(acc_full, ti & 1));  // tcgen05.ld is .sync.aligned
             if (!ok) break;
             tc_fence_after();
             const int row = n0 + q * 32 + lane;
+            const bool piece = kb0 != 0 || kb1 != kblocks;
+            float *slot = ws + (2 * (size_t)blockIdx.x + (pi == 0 ? 0 : 1)) * (size_t)(bx * kBN);
 #pragma unroll 1
             for (int c = 0; c < bx / 32; ++c) {
                 uint32_t v[32];
                 tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + c * 32, v);
                 tc_wait_ld();
-                if (row < n) y.store_run(m0 + c * 32, m, row, v);
+                if (piece)
+                    store_piece(slot, c, q * 32 + lane, v);
+                else if (row < n)
+                    y.store_run(m0 + c * 32, m, row, v);
             }
             tc_fence_before();
             __syncwarp();
@@ -475,83 +605,129 @@ inline int wide_nb(int64_t m) {
     return (int)std::min<int64_t>(kWideMaxNB, cdiv(cdiv(cdiv(m, tiles_m), 2), 16) * 16);
 }
 
-// Wide or 256-row tiles: a wave model of the persistent grid -- rounds of
-// tiles over the SMs, each tile costing its batch rows plus the dequant of
-// its weight tile (about 128 rows' worth, measured) -- which picks the
-// faster kind on every prefill shape measured (the wide tiles lose where
-// they leave too few tiles for the last round, e.g. N = 8192 at M = 1024).
-inline bool use_wide_tiles(int64_t m, int64_t n) {
-    if (m < kWideMinM) return false;
-    constexpr int64_t kDequantRows = 128;
-    const int64_t sms = sm_count(), tiles_n = cdiv(n, kBN), nb = wide_nb(m);
-    const int64_t narrow = cdiv(tiles_n * cdiv(m, kBX), sms) * (kBX + kDequantRows);
-    const int64_t wide = cdiv(tiles_n * cdiv(m, 2 * nb), sms) * (2 * nb + kDequantRows);
-    return wide < narrow;
-}
+// The launch plan: 256-row or wide tiles, and whether the tiles of the last
+// round are split (stream-K).  A wave model of the persistent grid picks it:
+// each tile costs its batch rows plus the dequant of its weight tile (about
+// 128 rows' worth, measured); whole tiles go in rounds over the SMs, the last
+// round often part-empty (148 SMs divide few tile counts); the split spreads
+// that last round's tiles evenly over all SMs.  Measured on the Llama-3-70B
+// MLP shapes, the split costs about a quarter round more than that (the
+// pieces' epilogues, the fix-up launch, and x streamed out of step with the
+// other SMs), and it only pays when the last round would be less than ~45 %
+// full: from 0.89 to 1.03 PFLOP/s (gate/up at M = 512, 4 of 448 tiles left
+// over), 0.92 -> 1.23 (down, M = 2048), 1.07 -> 1.17 (down, M = 8192); with
+// 57-86 % full last rounds it lost 0-9 %.  The split needs a caller
+// workspace of ws_bytes.
+struct GemmPlan {
+    bool wide = false, split = false;
+    int nb = 0, bx = kBX;
+    int64_t tiles = 0, grid = 0, kblocks = 0, t0 = 0;  // t0: first split tile (tiles: none)
+    size_t ws_bytes = 0;
+};
 
-template <typename XT>
-int launch_wide(const XT *x, CUtensorMapDataType xtype, const uint8_t *packed, const float *scales, OutSpec y,
-                int64_t m, int64_t n, int64_t k, int g, cudaStream_t st) {
-    const int64_t kp = cdiv(k, g) * g;
-    const int nb = wide_nb(m);
-    CUtensorMap xmap, wmap;
-    int rc = make_tensor_map_2d(&xmap, x, xtype, 2, (uint64_t)k, (uint64_t)m, (uint64_t)(k * 2), kBK, (uint32_t)nb,
-                                CU_TENSOR_MAP_SWIZZLE_128B);
-    if (rc != OQ_OK) return rc;
-    rc = make_tensor_map_2d(&wmap, packed, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)(kp / 2), (uint64_t)n,
-                            (uint64_t)(kp / 2), kBK / 2, kBN, CU_TENSOR_MAP_SWIZZLE_NONE);
-    if (rc != OQ_OK) return rc;
-    auto kern = gemm_int4_tcgen05_wide_kernel<XT>;
-    rc = allow_smem(reinterpret_cast<const void *>(kern), kWideSmemBytes);
-    if (rc != OQ_OK) return rc;
-    const int64_t tiles = cdiv(n, kBN) * cdiv(m, 2 * (int64_t)nb);
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)std::min<int64_t>(tiles, sm_count()));
-    cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = kWideSmemBytes;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    cudaError_t err = cudaLaunchKernelEx(&cfg, kern, xmap, wmap, scales, y, (int)m, (int)n, (int)kp, g, nb);
-    if (err != cudaSuccess) {
-        set_error("int4_linear (tcgen05 GEMM, wide tiles): launch failed: %s", cudaGetErrorString(err));
-        return OQ_ERR_CUDA;
+inline GemmPlan plan_gemm(int64_t m, int64_t n, int64_t k, int g, bool allow_split) {
+    constexpr int64_t kDequantRows = 128;
+    constexpr double kSplitOverhead = 0.25;  // rounds
+    constexpr double kSplitMaxLastRound = 0.45;
+    const int64_t sms = sm_count(), tiles_n = cdiv(n, kBN);
+    const int64_t kblocks = cdiv(cdiv(k, g) * g, kBK);
+    GemmPlan best;
+    double best_cost = 0.0;
+    auto consider = [&](bool wide, int nb, int bx, bool split) {
+        const int64_t tiles = tiles_n * cdiv(m, bx);
+        const double per_tile = (double)(bx + kDequantRows);
+        int64_t grid = std::min<int64_t>(tiles, sms), t0 = tiles;
+        double cost = per_tile * (double)cdiv(tiles, sms);
+        if (split) {
+            t0 = tiles / sms * sms;  // whole rounds first
+            const int64_t rest = tiles - t0;
+            grid = std::min<int64_t>(std::min<int64_t>(sms, kMaxPiecesPerTile - 1), rest * kblocks + t0);
+            if (rest == 0 || rest * kblocks < grid) return;  // nothing to split, or pieces under a k-block
+            if ((double)rest / (double)sms > kSplitMaxLastRound) return;
+            cost = per_tile * ((double)(t0 / sms) + (double)rest / (double)sms + kSplitOverhead);
+        }
+        if (best.tiles != 0 && cost >= best_cost) return;
+        best_cost = cost;
+        best.wide = wide, best.split = split, best.nb = nb, best.bx = bx, best.tiles = tiles, best.kblocks = kblocks;
+        best.grid = grid, best.t0 = t0;
+        best.ws_bytes = split ? (size_t)2 * grid * bx * kBN * sizeof(float) : 0;
+    };
+    consider(false, 0, kBX, false);
+    if (m >= kWideMinM) consider(true, wide_nb(m), 2 * wide_nb(m), false);
+    if (allow_split) {
+        consider(false, 0, kBX, true);
+        if (m >= kWideMinM) consider(true, wide_nb(m), 2 * wide_nb(m), true);
     }
-    return OQ_OK;
+    return best;
 }
 
 template <typename XT>
 int launch(const XT *x, CUtensorMapDataType xtype, const uint8_t *packed, const float *scales, OutSpec y, int64_t m,
-           int64_t n, int64_t k, int g, cudaStream_t st) {
-    if (use_wide_tiles(m, n)) return launch_wide(x, xtype, packed, scales, y, m, n, k, g, st);
+           int64_t n, int64_t k, int g, void *ws, size_t ws_bytes, cudaStream_t st) {
+    GemmPlan plan = plan_gemm(m, n, k, g, ws != nullptr);
+    if (plan.split && ws_bytes < plan.ws_bytes) plan = plan_gemm(m, n, k, g, false);
     const int64_t kp = cdiv(k, g) * g;
     CUtensorMap xmap, wmap;
-    int rc = make_tensor_map_2d(&xmap, x, xtype, 2, (uint64_t)k, (uint64_t)m, (uint64_t)(k * 2), kBK, kBX,
-                                CU_TENSOR_MAP_SWIZZLE_128B);
+    int rc = make_tensor_map_2d(&xmap, x, xtype, 2, (uint64_t)k, (uint64_t)m, (uint64_t)(k * 2), kBK,
+                                (uint32_t)(plan.wide ? plan.nb : kBX), CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc != OQ_OK) return rc;
     rc = make_tensor_map_2d(&wmap, packed, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)(kp / 2), (uint64_t)n,
                             (uint64_t)(kp / 2), kBK / 2, kBN, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc != OQ_OK) return rc;
-    auto kern = gemm_int4_tcgen05_kernel<XT>;
-    rc = allow_smem(reinterpret_cast<const void *>(kern), kSmemBytes);
-    if (rc != OQ_OK) return rc;
-    const int64_t tiles = cdiv(n, kBN) * cdiv(m, kBX);
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)std::min<int64_t>(tiles, sm_count()));
+    cfg.gridDim = dim3((unsigned)plan.grid);
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = kSmemBytes;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t err = cudaLaunchKernelEx(&cfg, kern, xmap, wmap, scales, y, (int)m, (int)n, (int)kp, g);
+    float *wsf = static_cast<float *>(ws);
+    cudaError_t err;
+    if (plan.wide) {
+        auto kern = gemm_int4_tcgen05_wide_kernel<XT>;
+        rc = allow_smem(reinterpret_cast<const void *>(kern), kWideSmemBytes);
+        if (rc != OQ_OK) return rc;
+        cfg.dynamicSmemBytes = kWideSmemBytes;
+        err = cudaLaunchKernelEx(&cfg, kern, xmap, wmap, scales, y, (int)m, (int)n, (int)kp, g, plan.nb, (int)plan.t0,
+                                 wsf);
+    } else {
+        auto kern = gemm_int4_tcgen05_kernel<XT>;
+        rc = allow_smem(reinterpret_cast<const void *>(kern), kSmemBytes);
+        if (rc != OQ_OK) return rc;
+        cfg.dynamicSmemBytes = kSmemBytes;
+        err = cudaLaunchKernelEx(&cfg, kern, xmap, wmap, scales, y, (int)m, (int)n, (int)kp, g, (int)plan.t0, wsf);
+    }
     if (err != cudaSuccess) {
         set_error("int4_linear (tcgen05 GEMM): launch failed: %s", cudaGetErrorString(err));
+        return OQ_ERR_CUDA;
+    }
+    if (!plan.split || plan.grid < 2) return OQ_OK;
+    // The split tiles, each by the first CTA boundary inside it.
+    const int64_t split_units = (plan.tiles - plan.t0) * plan.kblocks;
+    FixupList first = {};
+    int split_tiles = 0;
+    int64_t last = -1;
+    for (int64_t c = 1; c < plan.grid; ++c) {
+        const int64_t ub = split_units * c / plan.grid;
+        if (ub % plan.kblocks != 0 && ub / plan.kblocks != last) {
+            first.c[split_tiles++] = (int16_t)c;
+            last = ub / plan.kblocks;
+        }
+    }
+    if (split_tiles == 0) return OQ_OK;
+    // Chunks per split tile: about four CTAs per SM over all split tiles.
+    const int64_t chunks = std::min<int64_t>(256, std::max<int64_t>(4, cdiv(4 * sm_count(), split_tiles)));
+    cudaLaunchConfig_t fcfg = cfg;
+    fcfg.gridDim = dim3((unsigned)split_tiles, (unsigned)chunks);
+    fcfg.blockDim = dim3(256);
+    fcfg.dynamicSmemBytes = 0;
+    err = cudaLaunchKernelEx(&fcfg, streamk_fixup_kernel, (const float *)wsf, y, (int)m, (int)n,
+                             (int)cdiv(m, plan.bx), plan.bx, (int)plan.kblocks, (int)plan.t0, split_units,
+                             (int)plan.grid, first);
+    if (err != cudaSuccess) {
+        set_error("int4_linear (tcgen05 GEMM fix-up): launch failed: %s", cudaGetErrorString(err));
         return OQ_ERR_CUDA;
     }
     return OQ_OK;
@@ -574,11 +750,16 @@ int gemm_tcgen05_supported(int64_t m, int64_t n, int64_t k, int g, const void *x
 }
 
 int gemm_tcgen05_launch(const void *x, int x_dtype, const uint8_t *packed, const float *scales, OutSpec y, int64_t m,
-                        int64_t n, int64_t k, int g, cudaStream_t st) {
+                        int64_t n, int64_t k, int g, void *ws, size_t ws_bytes, cudaStream_t st) {
     if (x_dtype == OQ_BF16)
         return launch(static_cast<const __nv_bfloat16 *>(x), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, packed, scales, y, m,
-                      n, k, g, st);
-    return launch(static_cast<const __half *>(x), CU_TENSOR_MAP_DATA_TYPE_FLOAT16, packed, scales, y, m, n, k, g, st);
+                      n, k, g, ws, ws_bytes, st);
+    return launch(static_cast<const __half *>(x), CU_TENSOR_MAP_DATA_TYPE_FLOAT16, packed, scales, y, m, n, k, g, ws,
+                  ws_bytes, st);
+}
+
+size_t gemm_tcgen05_workspace_bytes(int64_t m, int64_t n, int64_t k, int g) {
+    return plan_gemm(m, n, k, g, true).ws_bytes;
 }
 
 }  // namespace oq

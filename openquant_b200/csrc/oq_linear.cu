@@ -17,7 +17,8 @@ namespace oq {
 int gemm_tcgen05_supported(int64_t m, int64_t n, int64_t k, int g, const void *x, const uint8_t *packed,
                            const float *y);
 int gemm_tcgen05_launch(const void *x, int x_dtype, const uint8_t *packed, const float *scales, OutSpec y,
-                        int64_t m, int64_t n, int64_t k, int g, cudaStream_t st);
+                        int64_t m, int64_t n, int64_t k, int g, void *ws, size_t ws_bytes, cudaStream_t st);
+size_t gemm_tcgen05_workspace_bytes(int64_t m, int64_t n, int64_t k, int g);
 
 namespace {
 
@@ -1512,8 +1513,19 @@ using namespace oq;
 namespace oq {
 namespace {
 
+// The kernel the automatic choice (and an explicit `kernel`) runs.
+int choose_kernel(int64_t m, int64_t n, int64_t k, int group_size, const void *x, const uint8_t *packed,
+                  int kernel) {
+    if (kernel != OQ_KERNEL_AUTO) return kernel;
+    const bool gemv_ok = gemv_supported(m, n, k, group_size, x, packed);
+    if (gemv_ok && m <= 16) return OQ_KERNEL_GEMV;
+    if (gemm_tcgen05_supported(m, n, k, group_size, x, packed, nullptr)) return OQ_KERNEL_TCGEN05;
+    return gemv_ok ? OQ_KERNEL_GEMV : OQ_KERNEL_SIMT;
+}
+
 int int4_linear_impl(const void *x, int x_dtype, const uint8_t *packed, const float *scales, OutSpec y, int64_t m,
-                     int64_t n, int64_t k, int group_size, int kernel, int config, oq_stream_t stream) {
+                     int64_t n, int64_t k, int group_size, int kernel, int config, void *ws, size_t ws_bytes,
+                     oq_stream_t stream) {
     OQ_REQUIRE(x_dtype == OQ_F16 || x_dtype == OQ_BF16, "Input must be a 2D FP16 or BF16 tensor");
     OQ_REQUIRE(group_size >= 2 && group_size % 2 == 0, "Group size must be even and >= 2");
     OQ_REQUIRE(m >= 1 && n >= 1 && k >= 1, "Matrix dimensions must be positive");
@@ -1534,17 +1546,7 @@ int int4_linear_impl(const void *x, int x_dtype, const uint8_t *packed, const fl
                                 config, st);
     }
     const bool gemv_ok = gemv_supported(m, n, k, group_size, x, packed);
-    int which = kernel;
-    if (which == OQ_KERNEL_AUTO) {
-        if (gemv_ok && m <= 16)
-            which = OQ_KERNEL_GEMV;
-        else if (gemm_tcgen05_supported(m, n, k, group_size, x, packed, nullptr))
-            which = OQ_KERNEL_TCGEN05;
-        else if (gemv_ok)
-            which = OQ_KERNEL_GEMV;
-        else
-            which = OQ_KERNEL_SIMT;
-    }
+    const int which = choose_kernel(m, n, k, group_size, x, packed, kernel);
     switch (which) {
         case OQ_KERNEL_GEMV:
             OQ_REQUIRE(gemv_ok, "GEMV kernel needs M <= 64, a power-of-two group_size >= 32, K % 8 == 0, 16-byte aligned x/packed, and x staged in shared memory or K a multiple of 128 and of the group");
@@ -1556,7 +1558,7 @@ int int4_linear_impl(const void *x, int x_dtype, const uint8_t *packed, const fl
         case OQ_KERNEL_TCGEN05:
             OQ_REQUIRE(gemm_tcgen05_supported(m, n, k, group_size, x, packed, nullptr),
                        "tcgen05 kernel does not support this shape/alignment");
-            return gemm_tcgen05_launch(x, x_dtype, packed, scales, y, m, n, k, group_size, st);
+            return gemm_tcgen05_launch(x, x_dtype, packed, scales, y, m, n, k, group_size, ws, ws_bytes, st);
         case OQ_KERNEL_SIMT:
             if (x_dtype == OQ_F16)
                 return launch_simt(static_cast<const __half *>(x), packed, scales, y, m, n, k, kp, group_size, st);
@@ -1574,7 +1576,7 @@ extern "C" int oq_int4_linear(const void *x, int x_dtype, const uint8_t *packed,
                               oq_stream_t stream) {
     clear_error();
     return int4_linear_impl(x, x_dtype, packed, scales, OutSpec{y, nullptr, OQ_F32}, m, n, k, group_size, kernel,
-                            config, stream);
+                            config, nullptr, 0, stream);
 }
 
 extern "C" int oq_int4_linear_ex(const void *x, int x_dtype, const uint8_t *packed, const float *scales, void *y,
@@ -1582,13 +1584,35 @@ extern "C" int oq_int4_linear_ex(const void *x, int x_dtype, const uint8_t *pack
                                  int kernel, int config, oq_stream_t stream) {
     clear_error();
     return int4_linear_impl(x, x_dtype, packed, scales, OutSpec{y, bias, y_dtype}, m, n, k, group_size, kernel,
-                            config, stream);
+                            config, nullptr, 0, stream);
+}
+
+extern "C" int oq_int4_linear_ws(const void *x, int x_dtype, const uint8_t *packed, const float *scales, void *y,
+                                 int y_dtype, const float *bias, int64_t m, int64_t n, int64_t k, int group_size,
+                                 int kernel, int config, void *workspace, size_t ws_bytes, oq_stream_t stream) {
+    clear_error();
+    OQ_REQUIRE(workspace == nullptr || aligned(workspace, 16), "workspace must be 16-byte aligned");
+    return int4_linear_impl(x, x_dtype, packed, scales, OutSpec{y, bias, y_dtype}, m, n, k, group_size, kernel,
+                            config, workspace, ws_bytes, stream);
+}
+
+extern "C" int64_t oq_int4_linear_workspace_bytes(int64_t m, int64_t n, int64_t k, int group_size, int kernel,
+                                                  int config) {
+    clear_error();
+    if (m < 1 || n < 1 || k < 1 || group_size < 2 || (config & OQ_CONFIG_SILU_GATE)) return 0;
+    // The GEMV and CUDA-core kernels take no workspace; the shapes the GEMM
+    // takes are alignment-independent apart from x / packed (16 bytes).
+    static const uint8_t aligned_probe[16] __attribute__((aligned(16))) = {};
+    const int which = choose_kernel(m, n, k, group_size, aligned_probe, aligned_probe, kernel);
+    if (which != OQ_KERNEL_TCGEN05 || !gemm_tcgen05_supported(m, n, k, group_size, aligned_probe, aligned_probe, nullptr))
+        return 0;
+    return (int64_t)gemm_tcgen05_workspace_bytes(m, n, k, group_size);
 }
 
 extern "C" int oq_int4_linear_peers(const void *x, int x_dtype, const uint8_t *packed, const float *scales,
                                     void *const *y_gpus, int n_gpus, int y_dtype, const float *bias, int64_t ld,
                                     int64_t col0, int64_t m, int64_t n, int64_t k, int group_size, int kernel,
-                                    int config, oq_stream_t stream) {
+                                    int config, void *workspace, size_t ws_bytes, oq_stream_t stream) {
     clear_error();
     OQ_REQUIRE(y_gpus != nullptr && n_gpus >= 1 && n_gpus <= kMaxOutGpus, "n_gpus must be in [1, %d]", kMaxOutGpus);
     OQ_REQUIRE(ld >= 1 && col0 >= 0 && col0 + n <= ld, "output columns [col0, col0 + n) must lie in a row of ld");
@@ -1601,5 +1625,7 @@ extern "C" int oq_int4_linear_peers(const void *x, int x_dtype, const uint8_t *p
         OQ_REQUIRE(y_gpus[i] != nullptr, "null output pointer for GPU %d", i);
         out.peer[i - 1] = y_gpus[i];
     }
-    return int4_linear_impl(x, x_dtype, packed, scales, out, m, n, k, group_size, kernel, config, stream);
+    OQ_REQUIRE(workspace == nullptr || aligned(workspace, 16), "workspace must be 16-byte aligned");
+    return int4_linear_impl(x, x_dtype, packed, scales, out, m, n, k, group_size, kernel, config, workspace, ws_bytes,
+                            stream);
 }

@@ -259,10 +259,13 @@ class ShardedInt4Linear:
         code = nat.OQ_F16 if x.dtype == torch.float16 else nat.OQ_BF16
 
         def run(sel, split):
+            ws_bytes = lib.oq_int4_linear_workspace_bytes(m, n_local, k, g, sel, split) if m > 16 else 0
+            ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device) if ws_bytes else None
             return lib.oq_int4_linear_peers(x.data_ptr(), code, self.local.data.data_ptr(),
                                             self.local.scales.data_ptr(), ys, world, _YCODES[out_dtype],
                                             bias.data_ptr() if bias is not None else None, self.n_total,
-                                            self.start, m, n_local, k, g, sel, split, stream)
+                                            self.start, m, n_local, k, g, sel, split,
+                                            ws.data_ptr() if ws is not None else None, ws_bytes, stream)
 
         status = run(sel, split)
         if status == nat.OQ_ERR_INVALID and (sel, split) != (0, 0):

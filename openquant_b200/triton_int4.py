@@ -14,7 +14,7 @@ import torch
 from . import _native as nat
 from . import tile_table
 
-__all__ = ["int4_linear"]
+__all__ = ["int4_linear", "Int4Linear"]
 
 _YCODES = {torch.float32: nat.OQ_F32, torch.float16: nat.OQ_F16, torch.bfloat16: nat.OQ_BF16}
 # The current stream's handle of a device without building a Stream object
@@ -141,6 +141,12 @@ def int4_linear(x, packed, scales, out_features, group_size, *, block_m=64, bloc
 
     def run(sel, split):
         stream = _stream_handle(dev)
+        ws_bytes = lib.oq_int4_linear_workspace_bytes(m, n, k, g, sel, split) if m > 16 else 0
+        if ws_bytes > 0:  # the prefill GEMM's even split of uneven tile counts (stream-K)
+            ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device)
+            return lib.oq_int4_linear_ws(ptrs[0], code, ptrs[1], ptrs[2], ptrs[3], ycodes[out.dtype],
+                                         bias.data_ptr() if bias is not None else None, m, n, k, g, sel, split,
+                                         ws.data_ptr(), ws_bytes, stream)
         if plain:
             return lib.oq_int4_linear(ptrs[0], code, ptrs[1], ptrs[2], ptrs[3], m, n, k, g, sel, split, stream)
         return lib.oq_int4_linear_ex(ptrs[0], code, ptrs[1], ptrs[2], ptrs[3], ycodes[out.dtype],
@@ -161,3 +167,119 @@ def int4_linear(x, packed, scales, out_features, group_size, *, block_m=64, bloc
         with torch.cuda.device(dev):
             launch()
     return out
+
+
+class Int4Linear:
+    """int4_linear for one fixed quantized weight, validated once.
+
+    A decode step calls the same layers over and over; this object checks
+    the weight-side arguments (packed, scales, out_features, group_size, bias,
+    out_dtype -- the preconditions of int4_linear, triton_int4.py:90-118 of
+    the reference) when it is made, and each call then checks only x (2-D
+    fp16 or bf16, contiguous, on the weights' GPU, K columns that pad to the
+    weights' KP) and launches the library's kernel directly -- the same
+    kernel and launch shape int4_linear chooses, so the same result bit for
+    bit.  `out`, when given, must be a contiguous (M, N) tensor of out_dtype
+    on that GPU; the call returns it (a new tensor otherwise).
+    """
+
+    def __init__(self, packed, scales, out_features, group_size, *, bias=None, out_dtype=torch.float32,
+                 exact_rounding=False, static_weights=False, kernel=None):
+        if not packed.is_cuda or not scales.is_cuda:
+            raise ValueError("All tensors must be on CUDA")
+        if packed.dtype != torch.uint8:
+            raise ValueError("Packed weights must be uint8")
+        if scales.dtype != torch.float32:
+            raise ValueError("Scales must be float32")
+        g = int(group_size)
+        if g < 2 or g % 2:
+            raise ValueError("Group size must be even and >= 2")
+        n = int(out_features)
+        if n < 1 or scales.ndim != 2 or int(scales.shape[0]) != n or int(scales.shape[1]) < 1:
+            raise ValueError("Incorrect scales shape")
+        kp = int(scales.shape[1]) * g
+        if packed.numel() != n * kp // 2:
+            raise ValueError("Incorrect packed weight count")
+        if not packed.is_contiguous() or not scales.is_contiguous():
+            raise ValueError("Weights and scales must be contiguous")
+        dev = packed.get_device()
+        if scales.get_device() != dev:
+            raise ValueError("All tensors must use the same GPU")
+        if out_dtype not in _YCODES:
+            raise ValueError("out_dtype must be torch.float32, torch.float16 or torch.bfloat16")
+        if bias is not None and (not isinstance(bias, torch.Tensor) or bias.dtype != torch.float32
+                                 or bias.numel() != n or bias.get_device() != dev or not bias.is_contiguous()):
+            raise ValueError("bias must be a contiguous float32 tensor of N elements on the weights' GPU")
+        if kernel is not None and kernel not in nat.KERNELS:
+            raise ValueError(f"unknown kernel {kernel!r}")
+        nat.require_device()
+        self.packed, self.scales, self.bias = packed, scales, bias
+        self.out_features, self.group_size, self.out_dtype = n, g, out_dtype
+        self._kp, self._dev, self._kernel = kp, dev, kernel
+        self._flags = (nat.CONFIG_EXACT_ROUNDING if exact_rounding else 0) | (
+            nat.CONFIG_STATIC_WEIGHTS if static_weights else 0)
+        self._lib = nat.load()
+        self._plain = bias is None and out_dtype == torch.float32
+        self._ptrs = (packed.data_ptr(), scales.data_ptr(), bias.data_ptr() if bias is not None else None)
+        self._ycode = _YCODES[out_dtype]
+        self._device = torch.device("cuda", dev)
+        self._shapes = {}  # m -> (kernel code, config, from the tuned table)
+
+    def _choice(self, m, k):
+        sel, split = (tile_table.lookup(m, self.out_features, k, self.group_size) if self._kernel is None
+                      else (nat.KERNELS[self._kernel], 0))
+        from_table = self._kernel is None and (sel, split & 15) != (0, 0)
+        cfg = split | self._flags
+        ws = self._lib.oq_int4_linear_workspace_bytes(m, self.out_features, k, self.group_size, sel, cfg) if m > 16 \
+            else 0
+        c = (sel, cfg, from_table, ws)
+        self._shapes[(m, k)] = c
+        return c
+
+    def __call__(self, x, out=None):
+        if x.dtype is torch.float16:
+            code = nat.OQ_F16
+        elif x.dtype is torch.bfloat16:
+            code = nat.OQ_BF16
+        else:
+            raise ValueError("Input must be a 2D FP16 tensor")
+        if x.ndim != 2 or not x.is_cuda or x.get_device() != self._dev or not x.is_contiguous():
+            raise ValueError("x must be a contiguous 2-D tensor on the weights' GPU")
+        m, k = x.shape
+        g = self.group_size
+        if m < 1 or (k + g - 1) // g * g != self._kp:
+            raise ValueError("x has the wrong number of columns for these weights")
+        n = self.out_features
+        if out is None:
+            out = torch.empty((m, n), device=self._device, dtype=self.out_dtype)
+        elif (out.dtype is not self.out_dtype or out.shape != (m, n) or out.get_device() != self._dev
+              or not out.is_contiguous()):
+            raise ValueError("out must be a contiguous (M, N) tensor of out_dtype on the weights' GPU")
+        if torch.cuda.current_device() != self._dev:  # the library launches on the current device
+            with torch.cuda.device(self._dev):
+                return self(x, out)
+        sel, cfg, from_table, ws_bytes = self._shapes.get((m, k)) or self._choice(m, k)
+        stream = _stream_handle(self._dev)
+        p, s, b = self._ptrs
+        if ws_bytes:  # the prefill GEMM's even split (stream-K) needs a workspace
+            ws = torch.empty(ws_bytes, dtype=torch.uint8, device=self._device)
+            st = self._lib.oq_int4_linear_ws(x.data_ptr(), code, p, s, out.data_ptr(), self._ycode, b, m, n, k, g,
+                                             sel, cfg, ws.data_ptr(), ws_bytes, stream)
+            if st == nat.OQ_ERR_INVALID and from_table:
+                st = self._lib.oq_int4_linear_ws(x.data_ptr(), code, p, s, out.data_ptr(), self._ycode, b, m, n, k,
+                                                 g, 0, cfg & ~15, ws.data_ptr(), ws_bytes, stream)
+        elif self._plain:
+            st = self._lib.oq_int4_linear(x.data_ptr(), code, p, s, out.data_ptr(), m, n, k, g, sel, cfg, stream)
+            if st == nat.OQ_ERR_INVALID and from_table:
+                st = self._lib.oq_int4_linear(x.data_ptr(), code, p, s, out.data_ptr(), m, n, k, g, 0, cfg & ~15,
+                                              stream)
+        else:
+            st = self._lib.oq_int4_linear_ex(x.data_ptr(), code, p, s, out.data_ptr(), self._ycode, b, m, n, k, g,
+                                             sel, cfg, stream)
+            if st == nat.OQ_ERR_INVALID and from_table:
+                st = self._lib.oq_int4_linear_ex(x.data_ptr(), code, p, s, out.data_ptr(), self._ycode, b, m, n, k,
+                                                 g, 0, cfg & ~15, stream)
+        if st:
+            nat.check(st)
+        return out
+

@@ -2,7 +2,7 @@
 
 Usage (in a container where the reference source tree is mounted):
 
-    python tests/golden/make_golden.py /root/reference
+    python tests/golden/make_golden.py <path of the reference source tree>
 
 It imports the reference's openquant package from the given tree, runs its
 NumPy quantizers / dequantizers and its torch decode helpers (on CPU
@@ -96,4 +96,6 @@ def main(ref_root):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py <path of the reference source tree>")
+    main(sys.argv[1])

@@ -351,6 +351,13 @@ def test_fused_bias_and_output_dtype(shape, out_dtype, kernel):
     out = torch.empty(m, n, dtype=out_dtype, device="cuda")
     assert int4_linear(xt, p, s, n, g, kernel=kernel, bias=bias, out=out) is out
     assert torch.equal(out, y)
+    # and directly against the oracle: (x . W^T + bias) within the parity bar,
+    # plus the output type's own rounding (half an ulp: 2^-11 fp16, 2^-8 bf16)
+    ref = orc.int4_linear(x, q.data, q.scales, n, g, x_dtype="f16") + bias.cpu().double().numpy()
+    rnd = {torch.float32: 0.0, torch.float16: 2.0 ** -11, torch.bfloat16: 2.0 ** -8}[out_dtype]
+    err = y.double().cpu().numpy() - ref
+    assert np.linalg.norm(err) / np.linalg.norm(ref) <= REL_L2 + rnd
+    assert (np.abs(err) <= MAX_ABS + rnd * np.abs(ref)).all()
 
 
 def test_fused_epilogue_every_gemv_config():
@@ -414,6 +421,20 @@ def test_silu_gate_fusion_matches_two_products(shape, dtype):
     assert float((err - 2e-6 * ref.abs()).max()) <= 1e-6, float(err.max())
     y = int4_linear(x, q.data, q.scales, n, g, silu_gate=True)
     assert y.shape == (m, n) and torch.equal(y, fused)
+    # directly against the oracle: silu(gate) * up from the oracle's two
+    # products in fp64.  Each product meets the parity bar (max-abs eps =
+    # 2e-2), so to first order |fused - ref| <= eps * (|silu'(g)| |u| +
+    # |silu(g)|), with |silu'| <= 1.1.
+    name = "f16" if dtype == torch.float16 else "bf16"
+    data, scales = q.data.cpu().numpy(), q.scales.cpu().numpy()
+    xf = x.float().cpu().numpy()
+    g_ref = orc.int4_linear(xf, data[:half], scales[:n], n, g, x_dtype=name)
+    u_ref = orc.int4_linear(xf, data[half:], scales[n:], n, g, x_dtype=name)
+    silu = g_ref / (1.0 + np.exp(-g_ref))
+    ref_o = silu * u_ref
+    err_o = fused.double().cpu().numpy() - ref_o
+    assert (np.abs(err_o) <= MAX_ABS * (1.1 * np.abs(u_ref) + np.abs(silu)) + 1e-6).all()
+    assert np.linalg.norm(err_o) / np.linalg.norm(ref_o) <= 2 * REL_L2
     yb = int4_linear(x, q.data, q.scales, n, g, silu_gate=True, out_dtype=torch.bfloat16)
     assert torch.equal(yb, fused.to(torch.bfloat16))
     with pytest.raises(ValueError):
@@ -438,3 +459,82 @@ def test_tile_table_entry_outside_its_plan_falls_back(monkeypatch):
     assert torch.equal(y, ref)
     check_against_oracle(y, x, q, g, torch.float16)
 
+
+
+@pytest.mark.parametrize("case", [(1, 4096, 4096, 128, torch.float16, {}),
+                                  (4, 4096, 12288, 128, torch.float16, {"static_weights": True}),
+                                  (16, 11008, 4096, 128, torch.float16, {"exact_rounding": True}),
+                                  (7, 1000, 300, 64, torch.bfloat16, {"out_dtype": torch.bfloat16, "bias": True}),
+                                  (300, 1024, 2048, 128, torch.bfloat16, {}),
+                                  (9, 200, 300, 6, torch.float16, {"kernel": "simt"})],
+                         ids=lambda c: f"m{c[0]}_n{c[1]}_k{c[2]}_g{c[3]}" if isinstance(c, tuple) else "")
+def test_int4_linear_layer_object_is_bit_equal(case):
+    """Int4Linear (validated once) launches what int4_linear launches: the
+    same output bits, call after call, with and without out=; and it refuses
+    an x that does not fit its weights."""
+    from openquant.groupwise import quantize_int4_groupwise
+    from openquant.triton_int4 import Int4Linear, int4_linear
+
+    m, n, k, g, dtype, opts = case
+    gen = torch.Generator(device="cuda").manual_seed(m * 7 + n)
+    q = quantize_int4_groupwise(torch.randn(n, k, device="cuda", generator=gen).mul_(0.02), g)
+    x = torch.randn(m, k, device="cuda", generator=gen).to(dtype)
+    opts = dict(opts)
+    if opts.pop("bias", False):
+        opts["bias"] = torch.randn(n, device="cuda", generator=gen)
+    layer = Int4Linear(q.data, q.scales, n, g, **opts)
+    ref = int4_linear(x, q.data, q.scales, n, g, **opts)
+    for _ in range(2):
+        assert torch.equal(layer(x), ref)
+    out = torch.empty_like(ref)
+    assert layer(x, out=out) is out and torch.equal(out, ref)
+    with pytest.raises(ValueError):
+        layer(torch.zeros(m, k + g, device="cuda", dtype=dtype))
+    with pytest.raises(ValueError):
+        layer(x.float())
+    with pytest.raises(ValueError):
+        layer(x, out=torch.empty(m, n + 1, device="cuda", dtype=ref.dtype))
+
+
+@pytest.mark.parametrize("case", [(300, 1000, 2048, 128, torch.bfloat16),   # 16 tiles, each cut over ~9 SMs
+                                  (77, 700, 1024, 64, torch.float16),
+                                  (300, 19456, 2048, 128, torch.bfloat16),  # 304 tiles: 2 rounds + 8 split
+                                  (1100, 2000, 512, 128, torch.bfloat16)],  # wide tiles, split
+                         ids=lambda c: f"m{c[0]}_n{c[1]}_k{c[2]}_g{c[3]}")
+def test_gemm_even_split_against_unsplit_and_oracle(case):
+    """The tcgen05 GEMM with a workspace splits the tiles' k-blocks evenly
+    over the SMs (stream-K) and adds the pieces in k order: deterministic
+    (two calls bit-equal), the unsplit kernel's result up to fp32 summation
+    order, the parity bar against the oracle, the fused epilogue (bias,
+    bf16 output) applied once to the added pieces; and with a workspace one
+    byte short it runs the unsplit kernel, bit for bit."""
+    from openquant_b200 import _native as nat
+
+    m, n, k, g, dtype = case
+    lib = nat.load()
+    x, q, xt = make_case(m, n, k, g, dtype, seed=m + k, w_sigma=0.02)
+    p, s = torch.from_numpy(q.data).cuda(), torch.from_numpy(q.scales).cuda()
+    code = nat.OQ_F16 if dtype == torch.float16 else nat.OQ_BF16
+    tc = nat.KERNELS["tcgen05"]
+    ws_bytes = lib.oq_int4_linear_workspace_bytes(m, n, k, g, tc, 0)
+    assert ws_bytes > 0, "this shape should take the split"
+    st = nat.stream_of(xt.device)
+
+    def run(ws_size, ydt=torch.float32, bias=None):
+        y = torch.full((m, n), float("nan"), device="cuda").to(ydt)
+        ws = torch.empty(max(ws_size, 16), dtype=torch.uint8, device="cuda")
+        nat.check(lib.oq_int4_linear_ws(nat.ptr(xt), code, nat.ptr(p), nat.ptr(s), nat.ptr(y),
+                                        {torch.float32: nat.OQ_F32, torch.bfloat16: nat.OQ_BF16}[ydt],
+                                        nat.ptr(bias) if bias is not None else None, m, n, k, g, tc, 0,
+                                        nat.ptr(ws), ws_size, st))
+        return y
+
+    y1, y2 = run(ws_bytes), run(ws_bytes)
+    assert torch.equal(y1, y2)
+    plain = torch.empty(m, n, device="cuda")
+    nat.check(lib.oq_int4_linear(nat.ptr(xt), code, nat.ptr(p), nat.ptr(s), nat.ptr(plain), m, n, k, g, tc, 0, st))
+    assert ((y1.double() - plain.double()).norm() / plain.double().norm()).item() < 1e-5
+    check_against_oracle(y1, x, q, g, dtype)
+    bias = torch.randn(n, device="cuda")
+    assert torch.equal(run(ws_bytes, torch.bfloat16, bias), (y1 + bias).to(torch.bfloat16))
+    assert torch.equal(run(ws_bytes - 1), plain)

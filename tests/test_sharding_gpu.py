@@ -89,7 +89,7 @@ def test_peers_entry_writes_every_buffer(case, y_dtype):
         order = [bufs[(r + j) % world] for j in range(world)]
         nat.check(lib.oq_int4_linear_peers(xt.data_ptr(), xcode, sh.data.data_ptr(), sh.scales.data_ptr(),
                                            _ptrs(order), world, ycode, bias[a:b].data_ptr(), n, a, m, b - a, k, g,
-                                           sel, 0, stream))
+                                           sel, 0, None, 0, stream))
         part = torch.empty((m, b - a), device="cuda", dtype=y_dtype)
         nat.check(lib.oq_int4_linear_ex(xt.data_ptr(), xcode, sh.data.data_ptr(), sh.scales.data_ptr(),
                                         part.data_ptr(), ycode, bias[a:b].data_ptr(), m, b - a, k, g, sel, 0, stream))
@@ -117,10 +117,10 @@ def test_peers_entry_rejects_bad_columns():
     stream = nat.stream_of(x.device)
     # columns [50, 114) do not fit a row of 100
     st = lib.oq_int4_linear_peers(x.data_ptr(), nat.OQ_F16, p.data_ptr(), s.data_ptr(), _ptrs([y]), 1, nat.OQ_F32,
-                                  None, 100, 50, 1, 64, 256, 128, 0, 0, stream)
+                                  None, 100, 50, 1, 64, 256, 128, 0, 0, None, 0, stream)
     assert st == nat.OQ_ERR_INVALID and "col0" in nat.last_error()
     st = lib.oq_int4_linear_peers(x.data_ptr(), nat.OQ_F16, p.data_ptr(), s.data_ptr(), _ptrs([y] * 9), 9, nat.OQ_F32,
-                                  None, 100, 0, 1, 64, 256, 128, 0, 0, stream)
+                                  None, 100, 0, 1, 64, 256, 128, 0, 0, None, 0, stream)
     assert st == nat.OQ_ERR_INVALID
 
 

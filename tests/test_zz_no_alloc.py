@@ -96,3 +96,31 @@ def test_sizes_beyond_the_fixed_array_are_rejected(lib):
         assert rc == nat.OQ_ERR_INVALID
         assert "fixed scratch" in nat.last_error()
     torch.cuda.synchronize()
+
+
+def test_calls_allocate_no_device_memory(lib):
+    """The defining property: once a shape has run (kernels loaded, the
+    array's address looked up), further calls leave the device's free memory
+    exactly where it was."""
+    from openquant_b200 import _native as nat
+
+    a = _case(nat, lib, 64, 512, 2048, torch.float16, seed=5)
+    b = _case(nat, lib, 5, 256, 4096, torch.bfloat16, seed=6)
+    ya, yb = torch.empty(64, 512, device="cuda"), torch.empty(5, 256, device="cuda")
+    st = nat.stream_of(ya.device)
+
+    def calls():
+        for (x, qw, sw), y in ((a, ya), (b, yb)):
+            m, k = x.shape
+            nat.check(lib.oq_int8_linear_noalloc(nat.ptr(x), _code(nat, x.dtype), nat.ptr(qw), nat.ptr(sw),
+                                                 nat.ptr(y), m, qw.shape[0], k, st))
+
+    calls()
+    torch.cuda.synchronize()
+    free_before = torch.cuda.mem_get_info()[0]
+    for _ in range(5):
+        calls()
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info()[0] == free_before
+    assert torch.equal(ya, _usual(nat, lib, *a)) and torch.equal(yb, _usual(nat, lib, *b))
+
