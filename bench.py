@@ -171,6 +171,8 @@ def summarize(line):
         elif wl.startswith("int4_linear_sharded"):
             out["sharded"] = {c: {k: r3(v[k]) for k in ("tflops", "us", "efficiency_vs_1gpu", "allgather_ms")
                                   if k in v} for c, v in a["by_case"].items()}
+        elif wl.startswith("int4_gemv_m1_k4096_n4096_g128_fp16_scales"):
+            out["gemv_fp16_scales"] = {"gbs": r3(a["value"]), "frac": r3(a["roofline"]["frac"])}
         elif wl.startswith("cpu_path_1024"):
             out["cpu_path_1024"] = {f: {"gpu_ms": r3(v["gpu_ms"]), "cpu_ms": r3(v["cpu_ms"]),
                                         "rel_weight_err": r3(v["rel_weight_err"])} for f, v in a["formats"].items()}
@@ -626,6 +628,78 @@ def measure_w8a8(dev, peaks, steps=10, warmup=3):
                      "algorithmic_ops_per_launch": 2 * m * n * k},
         "gpu_launches": steps,
         "check_max_rel_err": rel,
+    }
+
+
+def measure_gemv_fp16_scales(dev, peaks, steps=2000, warmup=100):
+    """The headline GEMV (M=1, K=N=4096, g=128, fp16 x) with one fp16 scale
+    per group (oq_int4_linear_f16s; the reference's format is fp32 scales):
+    the same packed weights, scales rounded to fp16, 64 copies rotated, static
+    weights, one CUDA graph of `steps` launches behind a device sleep, CUDA
+    events.  Checked against the oracle with the fp16 scales widened to fp32
+    (rel-L2 <= 1e-3, max-abs <= 2e-2)."""
+    import ctypes
+
+    import torch
+
+    from oq_oracle import int4_linear as orc_linear
+    from openquant_b200 import _native as nat
+    from openquant_b200.groupwise import quantize_int4_groupwise
+
+    lib = nat.load()
+    gen = torch.Generator(device=dev).manual_seed(4242)
+    packs, s16s = [], []
+    for _ in range(COPIES):
+        q = quantize_int4_groupwise(torch.randn(N, K, generator=gen, device=dev).mul_(0.02).half(), G)
+        packs.append(q.data)
+        s16s.append(q.scales.half())
+    x = torch.randn(M, K, generator=gen, device=dev).half()
+    y = torch.empty(M, N, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    torch.cuda.synchronize()
+
+    def launch(count, h, first=0):
+        for i in range(first, first + count):
+            st = lib.oq_int4_linear_f16s(ctypes.c_void_p(x.data_ptr()), nat.OQ_F16,
+                                         ctypes.c_void_p(packs[i % COPIES].data_ptr()),
+                                         ctypes.c_void_p(s16s[i % COPIES].data_ptr()), ctypes.c_void_p(y.data_ptr()),
+                                         nat.OQ_F32, None, M, N, K, G, nat.CONFIG_STATIC_WEIGHTS, h)
+            if st != 0:
+                raise RuntimeError(nat.last_error())
+
+    with torch.cuda.stream(stream):
+        launch(warmup, ctypes.c_void_p(stream.cuda_stream))
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        launch(steps, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream), first=warmup)
+    upload_graph(graph, stream)
+    torch.cuda.synchronize()
+    ms = _device_timed(stream, graph.replay, steps)
+    del graph
+    nbytes = N * KP // 2 + N * (KP // G) * 2 + M * K * 2 + M * N * 4
+    gbs = nbytes / (ms / 1e3) / 1e9
+    # parity: the last launch's copy against the oracle with the scales widened to fp32
+    last = (warmup + steps - 1) % COPIES
+    ref = orc_linear(x.float().cpu().numpy(), packs[last].cpu().numpy(), s16s[last].float().cpu().numpy(), N, G,
+                     x_dtype="f16")
+    err = y.double().cpu().numpy() - ref
+    rel = float(np.linalg.norm(err) / np.linalg.norm(ref))
+    mab = float(np.abs(err).max())
+    assert rel <= 1e-3 and mab <= 2e-2, (rel, mab)
+    return {
+        "metric": "INT4 GEMV GB/s at M=1, K=N=4096, g=128, one fp16 scale per group (variant)",
+        "workload": "int4_gemv_m1_k4096_n4096_g128_fp16_scales",
+        "value": gbs,
+        "unit": "GB/s",
+        "ms_per_step": ms,
+        "steps": steps,
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": gbs / peaks["hbm_gbs"], "algorithmic_bytes_per_launch": nbytes},
+        "vs_fp32_scales": "the headline line: same weights format but fp32 scales (8,937,472 B per launch)",
+        "gpu_launches": warmup + steps,
+        "check_rel_l2": rel,
+        "check_max_abs": mab,
     }
 
 
@@ -1358,6 +1432,7 @@ def run_ours(args):
         if not args.no_gemm:
             line["also"].append(measure_prefill_set(dev, peaks))
         line["also"].append(measure_cpu_path_1024(dev, peaks))
+        line["also"].append(measure_gemv_fp16_scales(dev, peaks))
     if not args.no_bulk:
         line.setdefault("also", []).append(measure_bulk_quant(dev, world, rank, peaks, layers=args.bulk_layers))
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -238,6 +238,22 @@ OQ_API int oq_int4_linear_ws(const void *x, int x_dtype, const uint8_t *packed,
                              void *workspace, size_t ws_bytes,
                              oq_stream_t stream);
 
+/* The fused INT4 linear layer with one fp16 scale per group: scales is
+ * fp16 [N][KP/g] (device) -- e.g. the fp32 scales of quantize_int4_groupwise
+ * rounded to fp16 -- and W[n][k] = int4(n, k) * (float)scales[n][k/g].  Runs
+ * the decode GEMV in its scale-after mode (each group's scale applied to the
+ * group's fp32 sum of x * q; the pair GEMV, else the TMA GEMV): fp16 x,
+ * M <= 16, a power-of-two group_size that is a multiple of 128, K % 8 == 0,
+ * 16-byte aligned x and packed, and x small enough for those kernels to stage
+ * it in shared memory (OQ_ERR_INVALID otherwise).  y, y_dtype and bias as oq_int4_linear_ex;
+ * config: OQ_CONFIG_STATIC_WEIGHTS only.  A variant of int4_linear,
+ * openquant/triton_int4.py:78-138, whose reference requires fp32 scales
+ * (:93-94): half the scale bytes per decode step. */
+OQ_API int oq_int4_linear_f16s(const void *x, int x_dtype, const uint8_t *packed,
+                               const void *scales, void *y, int y_dtype,
+                               const float *bias, int64_t m, int64_t n, int64_t k,
+                               int group_size, int config, oq_stream_t stream);
+
 /* Workspace bytes oq_int4_linear_ws uses for this shape and kernel choice
  * (0: the chosen kernel takes none).  Never fails (0 for invalid shapes). */
 OQ_API int64_t oq_int4_linear_workspace_bytes(int64_t m, int64_t n, int64_t k,

@@ -357,6 +357,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     }
 
+    // Lane 0 of warps 0 and 1 ran their roles alone: converge each warp
+    // before the CTA-wide barrier (an aligned barrier in a diverged warp is
+    // undefined), so that TMEM is released only after every role is done.
+    __syncwarp();
     __syncthreads();
     if (warp == 2) {
         tc_fence_after();
@@ -575,6 +579,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     }
 
+    // Lane 0 of warps 0 and 1 ran their roles alone: converge each warp
+    // before the CTA-wide barrier (an aligned barrier in a diverged warp is
+    // undefined), so that TMEM is released only after every role is done.
+    __syncwarp();
     __syncthreads();
     if (warp == 2) {
         tc_fence_after();

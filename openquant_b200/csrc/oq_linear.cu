@@ -98,6 +98,12 @@ __host__ __device__ constexpr size_t gemv_red_bytes(int warps, int nt) { return 
 // warp reads at one column fall in 8 bank groups instead of one.
 // Rows g and g + 8 share (row % 8), hence the swizzled column: both scales
 // of a lane come from one index computation.
+// One group scale from global memory: fp32 (the reference's format) or, with
+// half_scales, fp16 (the fp16-scale variant; `scales` then points at halves).
+__device__ __forceinline__ float load_scale(const float *scales, size_t idx, int half_scales) {
+    return half_scales ? __half2float(__ldg(reinterpret_cast<const __half *>(scales) + idx)) : __ldg(scales + idx);
+}
+
 __device__ __forceinline__ void stage_scales(const float *sst, int gi, int col, int spr, float &sa, float &sb) {
     const int c = spr == 32 ? ((((col >> 2) ^ (gi & 7)) << 2) | (col & 3)) : col;
     sa = sst[gi * spr + c];
@@ -477,7 +483,8 @@ template <typename XT, int NT, int CW, int CPW, bool SA, bool XS, bool STMA>
 __global__ void __launch_bounds__((CW + 1) * 32, CW <= 8 ? 2 : 1)
     gemv_tma_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap smap,
                     const XT *__restrict__ x, const float *__restrict__ scales, OutSpec y, int m, int n,
-                    int k, int kp, int gshift, int xstride, int nstages, int prefetch, int gate_n, int nred) {
+                    int k, int kp, int gshift, int xstride, int nstages, int prefetch, int gate_n, int nred,
+                    int half_scales) {
     static_assert(!SA || std::is_same<XT, __half>::value, "scale-after mode is for fp16 x");
     using L = TmaGemvLayout<CW, CPW>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -593,8 +600,8 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW <= 8 ? 2 : 1)
             for (int q = 0; q < CPW; ++q) {
                 const int c = st * CW * CPW + warp + q * CW;
                 const int col = min((128 * c + 32 * t) >> gshift, groups - 1);
-                sreg[q][0] = __ldg(scales + (size_t)ra * groups + col);
-                sreg[q][1] = __ldg(scales + (size_t)rb * groups + col);
+                sreg[q][0] = load_scale(scales, (size_t)ra * groups + col, half_scales);
+                sreg[q][1] = load_scale(scales, (size_t)rb * groups + col, half_scales);
             }
         }
         // warp-uniform: ldmatrix and mma.sync below are warp-collective
@@ -859,7 +866,7 @@ template <typename XT, int NT, bool SA, bool XS, bool STMA>
 __global__ void __launch_bounds__(512, 2)
     gemv_pair_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap smap,
                      const XT *__restrict__ x, const float *__restrict__ scales, OutSpec y, int m, int n,
-                     int k, int kp, int gshift, int xstride, int prefetch) {
+                     int k, int kp, int gshift, int xstride, int prefetch, int half_scales) {
     static_assert(!SA || std::is_same<XT, __half>::value, "scale-after mode is for fp16 x");
     constexpr int CW = 8, CPW = 4;
     using L = TmaGemvLayout<CW, CPW>;
@@ -939,8 +946,8 @@ __global__ void __launch_bounds__(512, 2)
         for (int q = 0; q < CPW; ++q) {
             const int c = wg + q * CW;
             const int col = min((128 * c + 32 * t) >> gshift, groups - 1);
-            sreg[q][0] = __ldg(scales + (size_t)ra * groups + col);
-            sreg[q][1] = __ldg(scales + (size_t)rb * groups + col);
+            sreg[q][0] = load_scale(scales, (size_t)ra * groups + col, half_scales);
+            sreg[q][1] = load_scale(scales, (size_t)rb * groups + col, half_scales);
         }
     }
     const bool ok = __all_sync(0xffffffffu, mbar_wait(&full[grp], 0));  // warp-uniform, as above
@@ -1183,7 +1190,8 @@ int make_gemv_maps(const uint8_t *packed, const float *scales, int64_t n, int64_
 
 template <typename XT, int NT, int CW, int CPW, bool SA, int CTAS = 1>
 int launch_gemv_tma(const XT *x, const uint8_t *packed, const float *scales, OutSpec y, int64_t m, int64_t n,
-                    int64_t k, int64_t kp, int g, int gshift, int prefetch, cudaStream_t st, int64_t gate_n = 0) {
+                    int64_t k, int64_t kp, int g, int gshift, int prefetch, cudaStream_t st, int64_t gate_n = 0,
+                    bool half_scales = false) {
     using L = TmaGemvLayout<CW, CPW>;
     size_t smem = 0;
     int xstride = 0;
@@ -1200,6 +1208,7 @@ int launch_gemv_tma(const XT *x, const uint8_t *packed, const float *scales, Out
     bool stma = false;
     const int rc = make_gemv_maps<CW, CPW>(packed, scales, n, kp, g, &wmap, &smap, &stma);
     if (rc != OQ_OK) return rc;
+    if (half_scales) stma = false;  // fp16 scales: each lane loads its own
     auto pick = [&](auto kern) -> int {
         int rc2 = allow_max_smem(reinterpret_cast<const void *>(kern));
         if (rc2 != OQ_OK) return rc2;
@@ -1214,7 +1223,8 @@ int launch_gemv_tma(const XT *x, const uint8_t *packed, const float *scales, Out
         cfg.attrs = attr;
         cfg.numAttrs = 1;
         cudaError_t err = cudaLaunchKernelEx(&cfg, kern, wmap, smap, x, scales, y, (int)m, (int)n, (int)k, (int)kp,
-                                             gshift, xstride, stages, prefetch, (int)gate_n, nred);
+                                             gshift, xstride, stages, prefetch, (int)gate_n, nred,
+                                             half_scales ? 1 : 0);
         if (err != cudaSuccess) {
             set_error("int4_linear (TMA GEMV): launch failed: %s", cudaGetErrorString(err));
             return OQ_ERR_CUDA;
@@ -1287,7 +1297,8 @@ inline bool gemv_pair_ok(int64_t m, int64_t n, int64_t k, int64_t kp, int g, con
 
 template <typename XT, int NT, bool SA>
 int launch_gemv_pair(const XT *x, const uint8_t *packed, const float *scales, OutSpec y, int64_t m, int64_t n,
-                     int64_t k, int64_t kp, int g, int gshift, int prefetch, cudaStream_t st) {
+                     int64_t k, int64_t kp, int g, int gshift, int prefetch, cudaStream_t st,
+                     bool half_scales = false) {
     using L = TmaGemvLayout<8, 4>;
     if (!gemv_pair_ok(m, n, k, kp, g, packed)) return invalid("pair GEMV (config 13) does not take this shape");
     const int64_t xstride = cdiv(kp, 128) * 128 + gemv_xpad(g);
@@ -1303,6 +1314,7 @@ int launch_gemv_pair(const XT *x, const uint8_t *packed, const float *scales, Ou
     bool stma = false;
     int rc = make_gemv_maps<8, 4>(packed, scales, n, kp, g, &wmap, &smap, &stma);
     if (rc != OQ_OK) return rc;
+    if (half_scales) stma = false;  // fp16 scales: each lane loads its own
     auto pick = [&](auto kern) -> int {
         int rc2 = allow_dynamic_smem(reinterpret_cast<const void *>(kern), smem);
         if (rc2 != OQ_OK) return rc2;
@@ -1317,7 +1329,7 @@ int launch_gemv_pair(const XT *x, const uint8_t *packed, const float *scales, Ou
         cfg.attrs = attr;
         cfg.numAttrs = 1;
         cudaError_t err = cudaLaunchKernelEx(&cfg, kern, wmap, smap, x, scales, y, (int)m, (int)n, (int)k, (int)kp,
-                                             gshift, (int)xstride, prefetch);
+                                             gshift, (int)xstride, prefetch, half_scales ? 1 : 0);
         if (err != cudaSuccess) {
             set_error("int4_linear (pair GEMV): launch failed: %s", cudaGetErrorString(err));
             return OQ_ERR_CUDA;
@@ -1437,6 +1449,27 @@ int launch_gemv(const XT *x, const uint8_t *packed, const float *scales, OutSpec
             return launch_gemv_sa<XT, true>(shape, x, packed, scales, y, m, n, k, kp, g, gshift, pf, st);
     }
     return launch_gemv_sa<XT, false>(shape, x, packed, scales, y, m, n, k, kp, g, gshift, pf, st);
+}
+
+// fp16-scale variant (oq_int4_linear_f16s): fp16 x, scale-after mode (g % 128
+// == 0), M <= 16, on the pair GEMV when it takes the shape, else the TMA GEMV
+// with 16 consumer warps (or 8); each lane loads its rows' fp16 scales.
+int launch_gemv_f16s(const __half *x, const uint8_t *packed, const float *scales16, OutSpec y, int64_t m, int64_t n,
+                     int64_t k, int64_t kp, int g, int config, cudaStream_t st) {
+    int gshift = 0;
+    while ((1 << gshift) < g) ++gshift;
+    const int pf = (config & OQ_CONFIG_STATIC_WEIGHTS) != 0;
+    const bool two = m > 8;
+    if (gemv_pair_ok(m, n, k, kp, g, packed))
+        return two ? launch_gemv_pair<__half, 2, true>(x, packed, scales16, y, m, n, k, kp, g, gshift, pf, st, true)
+                   : launch_gemv_pair<__half, 1, true>(x, packed, scales16, y, m, n, k, kp, g, gshift, pf, st, true);
+    if (tma_gemv_ok<16, 2>(m, k, kp, g, packed))
+        return two ? launch_gemv_tma<__half, 2, 16, 2, true>(x, packed, scales16, y, m, n, k, kp, g, gshift, pf, st, 0, true)
+                   : launch_gemv_tma<__half, 1, 16, 2, true>(x, packed, scales16, y, m, n, k, kp, g, gshift, pf, st, 0, true);
+    if (tma_gemv_ok<8, 4>(m, k, kp, g, packed))
+        return two ? launch_gemv_tma<__half, 2, 8, 4, true>(x, packed, scales16, y, m, n, k, kp, g, gshift, pf, st, 0, true)
+                   : launch_gemv_tma<__half, 1, 8, 4, true>(x, packed, scales16, y, m, n, k, kp, g, gshift, pf, st, 0, true);
+    return invalid("fp16 scales: neither the pair nor the TMA GEMV takes this shape (x must fit in shared memory)");
 }
 
 // SiLU-gate mode (OQ_CONFIG_SILU_GATE): the TMA GEMV over the [gate; up]
@@ -1594,6 +1627,26 @@ extern "C" int oq_int4_linear_ws(const void *x, int x_dtype, const uint8_t *pack
     OQ_REQUIRE(workspace == nullptr || aligned(workspace, 16), "workspace must be 16-byte aligned");
     return int4_linear_impl(x, x_dtype, packed, scales, OutSpec{y, bias, y_dtype}, m, n, k, group_size, kernel,
                             config, workspace, ws_bytes, stream);
+}
+
+extern "C" int oq_int4_linear_f16s(const void *x, int x_dtype, const uint8_t *packed, const void *scales, void *y,
+                                   int y_dtype, const float *bias, int64_t m, int64_t n, int64_t k, int group_size,
+                                   int config, oq_stream_t stream) {
+    clear_error();
+    OQ_REQUIRE(x_dtype == OQ_F16, "fp16 scales take fp16 x");
+    OQ_REQUIRE(group_size >= 2 && group_size % 2 == 0, "Group size must be even and >= 2");
+    OQ_REQUIRE(m >= 1 && n >= 1 && k >= 1, "Matrix dimensions must be positive");
+    OQ_REQUIRE(x && packed && scales && y, "null pointer argument");
+    OQ_REQUIRE(y_dtype == OQ_F32 || y_dtype == OQ_F16 || y_dtype == OQ_BF16, "output dtype must be fp32, fp16 or bf16");
+    OQ_REQUIRE(aligned(scales, 2), "fp16 scales must be 2-byte aligned");
+    OQ_REQUIRE(m <= 16 && group_size % 128 == 0 && gemv_supported(m, n, k, group_size, x, packed),
+               "fp16 scales run on the decode GEMV: M <= 16, a power-of-two group size that is a multiple of 128, "
+               "K %% 8 == 0, 16-byte aligned x and packed");
+    OutSpec out{y, bias, y_dtype};
+    out.ld = n;
+    const int64_t kp = cdiv(k, group_size) * group_size;
+    return launch_gemv_f16s(static_cast<const __half *>(x), packed, static_cast<const float *>(scales), out, m, n, k,
+                            kp, group_size, config, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int64_t oq_int4_linear_workspace_bytes(int64_t m, int64_t n, int64_t k, int group_size, int kernel,

@@ -30,7 +30,7 @@ def _stream_handle(dev):
 
 def int4_linear(x, packed, scales, out_features, group_size, *, block_m=64, block_n=64, block_k=64, num_warps=4,
                 kernel=None, out=None, exact_rounding=False, static_weights=False, bias=None, out_dtype=None,
-                silu_gate=False):
+                silu_gate=False, fp16_scales=False):
     """y = x @ W^T in fp32, W[n, k] = round_x(int4(n, k) * scales[n, k // g]).
 
     Arguments and errors follow triton_int4.py:78-118 (ValueError for each
@@ -67,6 +67,13 @@ def int4_linear(x, packed, scales, out_features, group_size, *, block_m=64, bloc
     before any kernel still in flight on the stream (quantized at load time
     and synchronized): the decode GEMV then streams them while the previous
     kernel drains instead of after it.  Results are unchanged.
+
+    fp16_scales=True takes `scales` as fp16 (N, G) -- one fp16 scale per
+    group, half the scale bytes -- instead of the reference's fp32 (which
+    stays the default and the only format without the flag): the weights are
+    int4 * (float)scale, run on the decode GEMV's scale-after mode (fp16 x,
+    M <= 16, group_size a multiple of 128), which applies each scale to its
+    group's sum.
     """
     if x.ndim != 2 or x.dtype not in (torch.float16, torch.bfloat16):
         raise ValueError("Input must be a 2D FP16 tensor")
@@ -76,8 +83,8 @@ def int4_linear(x, packed, scales, out_features, group_size, *, block_m=64, bloc
         raise ValueError("Input must be contiguous")
     if packed.dtype != torch.uint8:
         raise ValueError("Packed weights must be uint8")
-    if scales.dtype != torch.float32:
-        raise ValueError("Scales must be float32")
+    if scales.dtype != (torch.float16 if fp16_scales else torch.float32):
+        raise ValueError("Scales must be float16 (fp16_scales=True)" if fp16_scales else "Scales must be float32")
     if group_size < 2 or group_size % 2:
         raise ValueError("Group size must be even and >= 2")
     m, k = (int(v) for v in x.shape)
@@ -118,6 +125,24 @@ def int4_linear(x, packed, scales, out_features, group_size, *, block_m=64, bloc
             raise ValueError("bias must be a contiguous float32 tensor of N elements on x's device")
 
     nat.require_device()
+    if fp16_scales:
+        if silu_gate or kernel not in (None, "gemv") or exact_rounding:
+            raise ValueError("fp16_scales runs the decode GEMV's scale-after mode (no silu_gate, exact_rounding or "
+                             "kernel choice)")
+        lib = nat.load()
+
+        def launch_f16s():
+            nat.check(lib.oq_int4_linear_f16s(x.data_ptr(), nat.OQ_F16 if x.dtype == torch.float16 else nat.OQ_BF16,
+                                              packed.data_ptr(), scales.data_ptr(), out.data_ptr(), ycodes[out.dtype],
+                                              bias.data_ptr() if bias is not None else None, m, n, k, g,
+                                              nat.CONFIG_STATIC_WEIGHTS if static_weights else 0, _stream_handle(dev)))
+
+        if torch.cuda.current_device() == dev:
+            launch_f16s()
+        else:
+            with torch.cuda.device(dev):
+                launch_f16s()
+        return out
     if silu_gate:
         if kernel not in (None, "gemv"):
             raise ValueError("silu_gate runs on the GEMV kernel")

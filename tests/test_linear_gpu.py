@@ -538,3 +538,32 @@ def test_gemm_even_split_against_unsplit_and_oracle(case):
     bias = torch.randn(n, device="cuda")
     assert torch.equal(run(ws_bytes, torch.bfloat16, bias), (y1 + bias).to(torch.bfloat16))
     assert torch.equal(run(ws_bytes - 1), plain)
+
+
+@pytest.mark.parametrize("shape", [(1, 4096, 4096, 128), (16, 12288, 4096, 128), (4, 4096, 11008, 128),
+                                   (5, 300, 1000, 128)],
+                         ids=lambda s: "m%d_n%d_k%d_g%d" % s)
+def test_fp16_scales_vs_oracle(shape):
+    """int4_linear(..., fp16_scales=True): one fp16 scale per group, on the
+    decode GEMV (the pair GEMV where it takes the shape, else the TMA GEMV).
+    The oracle is the reference's arithmetic with those scales widened to fp32
+    (W = round_fp16(q * s)); same parity bar."""
+    from openquant.triton_int4 import int4_linear
+
+    m, n, k, g = shape
+    x, q, xt = make_case(m, n, k, g, torch.float16, seed=n + k, w_sigma=0.02)
+    s16 = q.scales.astype(np.float16)
+    p = torch.from_numpy(q.data).cuda()
+    y = int4_linear(xt, p, torch.from_numpy(s16).cuda(), n, g, fp16_scales=True)
+    ref = orc.int4_linear(x, q.data, s16.astype(np.float32), n, g, x_dtype="f16")
+    err = y.cpu().double().numpy() - ref
+    assert np.linalg.norm(err) / np.linalg.norm(ref) <= REL_L2
+    assert np.abs(err).max() <= MAX_ABS
+    # the fp32-scale call with the same scales widened: the same sums up to the
+    # launch shape's fp32 summation order (the tuned table may pick another)
+    y32 = int4_linear(xt, p, torch.from_numpy(s16.astype(np.float32)).cuda(), n, g)
+    assert ((y.double() - y32.double()).norm() / y32.double().norm()).item() < 1e-4
+    with pytest.raises(ValueError):  # the reference's contract stays: fp32 scales without the flag
+        int4_linear(xt, p, torch.from_numpy(s16).cuda(), n, g)
+    with pytest.raises(ValueError):
+        int4_linear(xt.to(torch.bfloat16), p, torch.from_numpy(s16).cuda(), n, g, fp16_scales=True)
