@@ -6,10 +6,12 @@
  * of the OpenQuant quantize-and-multiply path, as hand-written sm_100a CUDA
  * kernels.  Every entry point:
  *
- *   - borrows caller-owned DEVICE pointers (inputs are never written);
+ *   - borrows caller-owned DEVICE pointers (inputs are never written;
+ *     oq_int4_linear_host takes page-locked HOST activations and output);
  *   - enqueues its kernels on the caller's CUDA stream (`stream`, a
  *     cudaStream_t passed as void*; NULL = the legacy default stream) and
- *     returns without synchronising;
+ *     returns without synchronising (oq_int4_linear_host and
+ *     oq_take_device_error excepted, as documented there);
  *   - allocates no device memory (oq_peer_alloc excepted: allocating is
  *     its job);
  *   - returns OQ_OK (0) or an error code; oq_last_error() then returns a
@@ -253,6 +255,26 @@ OQ_API int oq_int4_linear_f16s(const void *x, int x_dtype, const uint8_t *packed
                                const void *scales, void *y, int y_dtype,
                                const float *bias, int64_t m, int64_t n, int64_t k,
                                int group_size, int config, oq_stream_t stream);
+
+/* The fused INT4 linear layer on HOST activations and output: x (M*K fp16 or
+ * bf16) and y (M*N of y_dtype) are page-locked host memory (cudaHostAlloc /
+ * cudaHostRegister); packed / scales / bias are device memory and x_stage a
+ * device buffer of M*K*2 bytes (16-byte aligned; contents overwritten).  One
+ * small kernel copies x over the bus into x_stage and the layer kernel -- the
+ * one oq_int4_linear_ex launches for these arguments, its weights streaming
+ * meanwhile (programmatic dependent launch) -- writes y straight into host
+ * memory through its mapped address; the call returns once y holds the
+ * result (`stream` synchronized).  x must be 16-byte aligned.  Meant for
+ * decode steps (the prefill GEMM's split over a workspace is not used here).
+ * Every other argument as oq_int4_linear_ex, and the same result bit for bit.
+ * Replaces the host round trip of a reference caller,
+ * int4_linear(x.cuda(), ...).cpu() -- openquant/triton_int4.py:78-138, fed
+ * from host arrays by .cuda() copies as in openquant/fused_benchmark.py:53-70. */
+OQ_API int oq_int4_linear_host(const void *x, int x_dtype, const uint8_t *packed,
+                               const float *scales, void *y, int y_dtype,
+                               const float *bias, int64_t m, int64_t n, int64_t k,
+                               int group_size, int kernel, int config,
+                               void *x_stage, oq_stream_t stream);
 
 /* Workspace bytes oq_int4_linear_ws uses for this shape and kernel choice
  * (0: the chosen kernel takes none).  Never fails (0 for invalid shapes). */

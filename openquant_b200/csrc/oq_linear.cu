@@ -206,6 +206,51 @@ __device__ __forceinline__ void gemv_stage_x(const XT *__restrict__ x, XT *xs, f
     }
 }
 
+// The part of x one warp of the pair GEMV reads -- its chunks c = wg + 8 q
+// (q < 4, c < nchunks) of every row r < m -- staged as gemv_stage_x does
+// (same layout, same bias table entries, same summation order), so the warp
+// can start on its chunks after a __syncwarp instead of a barrier over the
+// whole CTA: the other warps' x loads no longer gate it.  Lane l stages
+// vectors l and l + 32 of the warp's 64 per row (chunk q = vector / 16), two
+// rows per pass, all four loads issued first.  Warps of the two tile groups
+// with the same wg write the same values.
+template <typename XT, bool SA, bool FOLD>
+__device__ __forceinline__ void gemv_stage_x_warp(const XT *__restrict__ x, XT *xs, float *corr, int m, int k,
+                                                  int xstride, int wg, int lane, int nchunks) {
+    const int kv = k / 8;
+    for (int r0 = 0; r0 < m; r0 += 2) {
+        uint4 v[2][2];
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int r = r0 + rr, i = lane + 32 * h, c = wg + 8 * (i >> 4), cv = 16 * c + (i & 15);
+                v[rr][h] = r < m && c < nchunks && cv < kv
+                               ? __ldg(reinterpret_cast<const uint4 *>(x) + (size_t)r * kv + cv)
+                               : make_uint4(0, 0, 0, 0);
+            }
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int r = r0 + rr, i = lane + 32 * h, c = wg + 8 * (i >> 4), cv = 16 * c + (i & 15);
+                const bool live = r < m && c < nchunks;
+                const uint4 w = SA ? sa_perm_x(v[rr][h]) : v[rr][h];
+                if (live) reinterpret_cast<uint4 *>(xs)[r * (xstride / 8) + cv] = w;
+                if (FOLD) {  // warp-uniform: every lane takes part in the shuffles
+                    const float2 f0 = __half22float2(*reinterpret_cast<const __half2 *>(&w.x));
+                    const float2 f1 = __half22float2(*reinterpret_cast<const __half2 *>(&w.y));
+                    const float2 f2 = __half22float2(*reinterpret_cast<const __half2 *>(&w.z));
+                    const float2 f3 = __half22float2(*reinterpret_cast<const __half2 *>(&w.w));
+                    float t = 1032.0f * ((f0.x + f0.y) + (f1.x + f1.y)) + 1152.0f * ((f2.x + f2.y) + (f3.x + f3.y));
+#pragma unroll
+                    for (int o = 8; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+                    if (live && (i & 15) == 0) corr[c * 16 + r] = t;
+                }
+            }
+    }
+}
+
 // FOLD (staged x only): the biased halves (1032 + q, 1152 + 16 q) go to the
 // tensor core as they are -- no HSUB2 -- and the bias's share of each sum,
 // 1032 * (sum of the chunk's class-0 x) + 1152 * (sum of its class-1 x / 16)
@@ -908,10 +953,12 @@ __global__ void __launch_bounds__(512, 2)
         }
     }
 
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-    if (XS) gemv_stage_x<XT, SA, FOLD>(x, xs, corr, m, k, kp, xstride, 512);
-    __syncthreads();  // xs staged; the barriers initialised before anyone waits on them
+    __syncthreads();  // the barriers initialised before anyone waits on them
     if (grp >= ntiles) return;  // no second tile: the second warp group is done
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    // Each warp stages the x its own chunks read: no CTA-wide barrier after the wait.
+    if (XS) gemv_stage_x_warp<XT, SA, FOLD>(x, xs, corr, m, k, xstride, wg, lane, nchunks);
+    __syncwarp();
 
     const uint8_t *wst = smem + grp * stage_pitch;
     const float *sst = reinterpret_cast<const float *>(wst + L::kStageBytes);
@@ -1647,6 +1694,63 @@ extern "C" int oq_int4_linear_f16s(const void *x, int x_dtype, const uint8_t *pa
     const int64_t kp = cdiv(k, group_size) * group_size;
     return launch_gemv_f16s(static_cast<const __half *>(x), packed, static_cast<const float *>(scales), out, m, n, k,
                             kp, group_size, config, static_cast<cudaStream_t>(stream));
+}
+
+namespace oq {
+namespace {
+// Device address of page-locked host memory (the same pointer on a
+// unified-address system), or nullptr when `p` is not page-locked and mapped.
+void *mapped_host_address(const void *p) {
+    cudaPointerAttributes attr{};
+    if (cudaPointerGetAttributes(&attr, p) != cudaSuccess) {
+        cudaGetLastError();  // pageable memory: not an error state to keep
+        return nullptr;
+    }
+    if (attr.type != cudaMemoryTypeHost || attr.devicePointer == nullptr) return nullptr;
+    return attr.devicePointer;
+}
+
+// Copies `bytes` from mapped host memory into device memory (both addresses
+// 16-byte aligned), 16 bytes per thread and the last bytes % 16 by thread 0:
+// one read of the activations over the bus per decode step, after which
+// every CTA of the layer kernel reads them from L2.  It lets the layer kernel
+// launch at once (programmatic dependent launch), so the kernel's static
+// weights stream from HBM while the activations cross the bus.
+__global__ void __launch_bounds__(256) host_to_device_kernel(const uint8_t *__restrict__ src,
+                                                              uint8_t *__restrict__ dst, int64_t bytes) {
+    asm volatile("griddepcontrol.launch_dependents;");
+    const int64_t n16 = bytes / 16;
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n16) reinterpret_cast<uint4 *>(dst)[i] = reinterpret_cast<const uint4 *>(src)[i];
+    if (i == 0)
+        for (int64_t b = n16 * 16; b < bytes; ++b) dst[b] = src[b];
+}
+}  // namespace
+}  // namespace oq
+
+extern "C" int oq_int4_linear_host(const void *x, int x_dtype, const uint8_t *packed, const float *scales, void *y,
+                                   int y_dtype, const float *bias, int64_t m, int64_t n, int64_t k, int group_size,
+                                   int kernel, int config, void *x_stage, oq_stream_t stream) {
+    clear_error();
+    OQ_REQUIRE(x && y && packed && scales && x_stage, "null pointer argument");
+    void *xd = mapped_host_address(x);
+    void *yd = mapped_host_address(y);
+    OQ_REQUIRE(xd != nullptr && yd != nullptr,
+               "x and y must be page-locked host memory (cudaHostAlloc / cudaHostRegister; torch: pin_memory())");
+    OQ_REQUIRE(x_dtype == OQ_F16 || x_dtype == OQ_BF16, "Input must be a 2D FP16 or BF16 tensor");
+    OQ_REQUIRE(m >= 1 && n >= 1 && k >= 1 && m < (1ll << 40) / k, "Matrix dimensions must be positive");
+    const int64_t xbytes = m * k * 2;
+    OQ_REQUIRE(aligned(xd, 16) && aligned(x_stage, 16), "host input: x and x_stage must be 16-byte aligned");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    host_to_device_kernel<<<(unsigned)std::max<int64_t>(1, cdiv(xbytes / 16, 256)), 256, 0, st>>>(
+        static_cast<const uint8_t *>(xd), static_cast<uint8_t *>(x_stage), xbytes);
+    int rc = check_launch("int4_linear (host input copy)");
+    if (rc != OQ_OK) return rc;
+    rc = int4_linear_impl(x_stage, x_dtype, packed, scales, OutSpec{yd, bias, y_dtype}, m, n, k, group_size, kernel,
+                          config, nullptr, 0, stream);
+    if (rc != OQ_OK) return rc;
+    OQ_CUDA(cudaStreamSynchronize(st));
+    return OQ_OK;
 }
 
 extern "C" int64_t oq_int4_linear_workspace_bytes(int64_t m, int64_t n, int64_t k, int group_size, int kernel,

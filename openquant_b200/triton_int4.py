@@ -249,6 +249,7 @@ class Int4Linear:
         self._ycode = _YCODES[out_dtype]
         self._device = torch.device("cuda", dev)
         self._shapes = {}  # m -> (kernel code, config, from the tuned table)
+        self._stages = {}  # (m, k) -> device copy of a host x (forward_host)
 
     def _choice(self, m, k):
         sel, split = (tile_table.lookup(m, self.out_features, k, self.group_size) if self._kernel is None
@@ -308,3 +309,45 @@ class Int4Linear:
             nat.check(st)
         return out
 
+    def forward_host(self, x, out=None):
+        """The layer on host tensors: x a contiguous (M, K) fp16 / bf16 CPU
+        tensor in page-locked memory (``pin_memory()``), the result written
+        into `out` -- a page-locked (M, N) CPU tensor of out_dtype, allocated
+        when None -- and returned once it is complete
+        (oq_int4_linear_host: a small kernel copies x over the bus into a
+        device buffer this object keeps per M, while the layer kernel's
+        weights stream; the layer kernel writes y straight into `out`).  The
+        same kernel and result as ``self(x.cuda()).cpu()`` -- bit for bit for
+        decode shapes; the prefill GEMM runs without its stream-K split.  The
+        weights' GPU must be the current device."""
+        # (page-locking of x and out is checked by the library, which refuses
+        # pageable memory with OQ_ERR_INVALID -> ValueError)
+        if x.dtype is torch.float16:
+            code = nat.OQ_F16
+        elif x.dtype is torch.bfloat16:
+            code = nat.OQ_BF16
+        else:
+            raise ValueError("Input must be a 2D FP16 tensor")
+        if x.ndim != 2 or x.is_cuda or not x.is_contiguous():
+            raise ValueError("x must be a contiguous 2-D CPU tensor in page-locked memory (pin_memory())")
+        m, k = x.shape
+        g, n = self.group_size, self.out_features
+        if m < 1 or (k + g - 1) // g * g != self._kp:
+            raise ValueError("x has the wrong number of columns for these weights")
+        if out is None:
+            out = torch.empty((m, n), dtype=self.out_dtype, pin_memory=True)
+        elif out.dtype is not self.out_dtype or out.shape != (m, n) or out.is_cuda or not out.is_contiguous():
+            raise ValueError("out must be a contiguous page-locked (M, N) CPU tensor of out_dtype")
+        stage = self._stages.get((m, k))
+        if stage is None:
+            stage = self._stages[(m, k)] = torch.empty((m, k), dtype=torch.float16, device=self._device)
+        sel, cfg, from_table, _ = self._shapes.get((m, k)) or self._choice(m, k)
+        p, s, b = self._ptrs
+        stream = _stream_handle(self._dev)
+        args = (x.data_ptr(), code, p, s, out.data_ptr(), self._ycode, b, m, n, k, g)
+        st = self._lib.oq_int4_linear_host(*args, sel, cfg, stage.data_ptr(), stream)
+        if st == nat.OQ_ERR_INVALID and from_table:
+            st = self._lib.oq_int4_linear_host(*args, 0, cfg & ~15, stage.data_ptr(), stream)
+        if st:
+            nat.check(st)
+        return out

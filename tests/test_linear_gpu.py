@@ -496,6 +496,53 @@ def test_int4_linear_layer_object_is_bit_equal(case):
         layer(x, out=torch.empty(m, n + 1, device="cuda", dtype=ref.dtype))
 
 
+@pytest.mark.parametrize("case", [(1, 4096, 4096, 128, torch.float16, {"static_weights": True}),
+                                  (4, 4096, 12288, 128, torch.float16, {}),
+                                  (16, 11008, 4096, 128, torch.float16, {"exact_rounding": True}),
+                                  (7, 1000, 300, 64, torch.bfloat16, {"out_dtype": torch.bfloat16, "bias": True}),
+                                  (9, 200, 300, 6, torch.float16, {"kernel": "simt"}),
+                                  (40, 512, 1024, 128, torch.bfloat16, {})],
+                         ids=lambda c: f"m{c[0]}_n{c[1]}_k{c[2]}_g{c[3]}" if isinstance(c, tuple) else "")
+def test_int4_linear_forward_host(case):
+    """Int4Linear.forward_host (oq_int4_linear_host): x and y in page-locked
+    host memory; a copy kernel brings x over the bus and the layer kernel
+    writes y into host memory.  For decode shapes the output equals the
+    device-buffer call's bit for bit; above M = 16 the prefill GEMM runs
+    without its stream-K split and meets the oracle bar.  Pageable host memory
+    and device tensors are refused."""
+    from openquant.groupwise import quantize_int4_groupwise
+    from openquant.triton_int4 import Int4Linear
+
+    m, n, k, g, dtype, opts = case
+    gen = torch.Generator(device="cuda").manual_seed(m * 5 + n)
+    w = torch.randn(n, k, device="cuda", generator=gen).mul_(0.02)
+    q = quantize_int4_groupwise(w, g)
+    x = torch.randn(m, k, device="cuda", generator=gen).to(dtype)
+    opts = dict(opts)
+    if opts.pop("bias", False):
+        opts["bias"] = torch.randn(n, device="cuda", generator=gen)
+    layer = Int4Linear(q.data, q.scales, n, g, **opts)
+    ref = layer(x).cpu()
+    x_host = x.cpu().pin_memory()
+    for _ in range(2):
+        got = layer.forward_host(x_host)
+        assert got.is_pinned() and got.dtype == ref.dtype and got.shape == ref.shape
+        if m <= 16:
+            assert torch.equal(got, ref)
+    out = torch.empty(ref.shape, dtype=ref.dtype, pin_memory=True)
+    assert layer.forward_host(x_host, out=out) is out and torch.equal(out, got)
+    if opts.get("bias") is None and ref.dtype == torch.float32:
+        qn = quantize_int4_groupwise(w.cpu().numpy(), g)
+        xn = x.float().cpu().numpy()
+        check_against_oracle(got, xn, qn, g, dtype)
+    with pytest.raises(ValueError, match="page-locked"):
+        layer.forward_host(x.cpu())
+    with pytest.raises(ValueError, match="page-locked"):
+        layer.forward_host(x_host, out=torch.empty(ref.shape, dtype=ref.dtype))
+    with pytest.raises(ValueError):
+        layer.forward_host(x)
+
+
 @pytest.mark.parametrize("case", [(300, 1000, 2048, 128, torch.bfloat16),   # 16 tiles, each cut over ~9 SMs
                                   (77, 700, 1024, 64, torch.float16),
                                   (300, 19456, 2048, 128, torch.bfloat16),  # 304 tiles: 2 rounds + 8 split
