@@ -10,8 +10,9 @@
  *     oq_int4_linear_host takes page-locked HOST activations and output);
  *   - enqueues its kernels on the caller's CUDA stream (`stream`, a
  *     cudaStream_t passed as void*; NULL = the legacy default stream) and
- *     returns without synchronising (oq_int4_linear_host and
- *     oq_take_device_error excepted, as documented there);
+ *     returns without synchronising (oq_int4_linear_host,
+ *     oq_int4_linear_host_run and oq_take_device_error excepted, as
+ *     documented there);
  *   - allocates no device memory (oq_peer_alloc excepted: allocating is
  *     its job);
  *   - returns OQ_OK (0) or an error code; oq_last_error() then returns a
@@ -275,6 +276,25 @@ OQ_API int oq_int4_linear_host(const void *x, int x_dtype, const uint8_t *packed
                                const float *bias, int64_t m, int64_t n, int64_t k,
                                int group_size, int kernel, int config,
                                void *x_stage, oq_stream_t stream);
+
+/* oq_int4_linear_host with its arguments fixed once: the copy kernel and the
+ * layer kernel are captured into a CUDA graph (on the current device), and
+ * oq_int4_linear_host_run replays it on `stream` and returns once y holds
+ * the result -- one graph launch and one synchronization per decode step.
+ * The graph reads x and writes y, x_stage (and reads packed, scales, bias) at
+ * the addresses given here each time it runs: they stay borrowed, must
+ * outlive the plan and keep their page-locking; their contents may change
+ * between runs.  Runs of one plan must not overlap.  *plan receives an
+ * opaque handle (NULL on failure); oq_int4_linear_host_plan_free releases it
+ * (NULL is a no-op).  Same validation, kernels and result as
+ * oq_int4_linear_host; no counterpart in the reference. */
+OQ_API int oq_int4_linear_host_plan(const void *x, int x_dtype, const uint8_t *packed,
+                                    const float *scales, void *y, int y_dtype,
+                                    const float *bias, int64_t m, int64_t n, int64_t k,
+                                    int group_size, int kernel, int config,
+                                    void *x_stage, void **plan);
+OQ_API int oq_int4_linear_host_run(void *plan, oq_stream_t stream);
+OQ_API int oq_int4_linear_host_plan_free(void *plan);
 
 /* Workspace bytes oq_int4_linear_ws uses for this shape and kernel choice
  * (0: the chosen kernel takes none).  Never fails (0 for invalid shapes). */

@@ -45,6 +45,10 @@ SIGNATURES = {
     "oq_int4_linear_workspace_bytes": (_I64, [_I64, _I64, _I64, _I32, _I32, _I32]),
     "oq_int4_linear_f16s": (_I32, [_P, _I32, _P, _P, _P, _I32, _P, _I64, _I64, _I64, _I32, _I32, _P]),
     "oq_int4_linear_host": (_I32, [_P, _I32, _P, _P, _P, _I32, _P, _I64, _I64, _I64, _I32, _I32, _I32, _P, _P]),
+    "oq_int4_linear_host_plan": (_I32, [_P, _I32, _P, _P, _P, _I32, _P, _I64, _I64, _I64, _I32, _I32, _I32, _P,
+                                        _P]),
+    "oq_int4_linear_host_run": (_I32, [_P, _P]),
+    "oq_int4_linear_host_plan_free": (_I32, [_P]),
     "oq_peer_alloc": (_I32, [ctypes.c_size_t, _P]),
     "oq_peer_free": (_I32, [_P]),
     "oq_peer_export": (_I32, [_P, _P]),

@@ -1728,10 +1728,13 @@ __global__ void __launch_bounds__(256) host_to_device_kernel(const uint8_t *__re
 }  // namespace
 }  // namespace oq
 
-extern "C" int oq_int4_linear_host(const void *x, int x_dtype, const uint8_t *packed, const float *scales, void *y,
-                                   int y_dtype, const float *bias, int64_t m, int64_t n, int64_t k, int group_size,
-                                   int kernel, int config, void *x_stage, oq_stream_t stream) {
-    clear_error();
+namespace oq {
+namespace {
+// Validates a host-buffer call and enqueues it on `st`: the copy kernel,
+// then the layer kernel writing y through its mapped address.
+int host_enqueue(const void *x, int x_dtype, const uint8_t *packed, const float *scales, void *y, int y_dtype,
+                 const float *bias, int64_t m, int64_t n, int64_t k, int group_size, int kernel, int config,
+                 void *x_stage, cudaStream_t st) {
     OQ_REQUIRE(x && y && packed && scales && x_stage, "null pointer argument");
     void *xd = mapped_host_address(x);
     void *yd = mapped_host_address(y);
@@ -1741,13 +1744,87 @@ extern "C" int oq_int4_linear_host(const void *x, int x_dtype, const uint8_t *pa
     OQ_REQUIRE(m >= 1 && n >= 1 && k >= 1 && m < (1ll << 40) / k, "Matrix dimensions must be positive");
     const int64_t xbytes = m * k * 2;
     OQ_REQUIRE(aligned(xd, 16) && aligned(x_stage, 16), "host input: x and x_stage must be 16-byte aligned");
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
     host_to_device_kernel<<<(unsigned)std::max<int64_t>(1, cdiv(xbytes / 16, 256)), 256, 0, st>>>(
         static_cast<const uint8_t *>(xd), static_cast<uint8_t *>(x_stage), xbytes);
-    int rc = check_launch("int4_linear (host input copy)");
+    const int rc = check_launch("int4_linear (host input copy)");
     if (rc != OQ_OK) return rc;
-    rc = int4_linear_impl(x_stage, x_dtype, packed, scales, OutSpec{yd, bias, y_dtype}, m, n, k, group_size, kernel,
-                          config, nullptr, 0, stream);
+    return int4_linear_impl(x_stage, x_dtype, packed, scales, OutSpec{yd, bias, y_dtype}, m, n, k, group_size, kernel,
+                            config, nullptr, 0, st);
+}
+
+// A captured host-buffer call (oq_int4_linear_host_plan).
+struct HostPlan {
+    cudaGraphExec_t exec = nullptr;
+    int device = -1;
+};
+}  // namespace
+}  // namespace oq
+
+extern "C" int oq_int4_linear_host_plan(const void *x, int x_dtype, const uint8_t *packed, const float *scales,
+                                        void *y, int y_dtype, const float *bias, int64_t m, int64_t n, int64_t k,
+                                        int group_size, int kernel, int config, void *x_stage, void **plan) {
+    clear_error();
+    OQ_REQUIRE(plan != nullptr, "null plan pointer");
+    *plan = nullptr;
+    int dev = 0;
+    OQ_CUDA(cudaGetDevice(&dev));
+    cudaStream_t cs = nullptr;
+    OQ_CUDA(cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking));
+    cudaGraph_t graph = nullptr;
+    cudaError_t err = cudaStreamBeginCapture(cs, cudaStreamCaptureModeRelaxed);
+    int rc = OQ_OK;
+    if (err == cudaSuccess) {
+        rc = host_enqueue(x, x_dtype, packed, scales, y, y_dtype, bias, m, n, k, group_size, kernel, config, x_stage,
+                          cs);
+        const cudaError_t end = cudaStreamEndCapture(cs, &graph);  // ends the capture whatever happened
+        if (rc == OQ_OK && end != cudaSuccess) err = end;
+    }
+    cudaGraphExec_t exec = nullptr;
+    if (err == cudaSuccess && rc == OQ_OK) err = cudaGraphInstantiate(&exec, graph, 0);
+    if (graph) cudaGraphDestroy(graph);
+    cudaStreamDestroy(cs);
+    if (rc != OQ_OK) return rc;
+    if (err != cudaSuccess) {
+        set_error("int4_linear host plan: graph capture failed: %s", cudaGetErrorString(err));
+        return OQ_ERR_CUDA;
+    }
+    auto *hp = new HostPlan;
+    hp->exec = exec;
+    hp->device = dev;
+    *plan = hp;
+    return OQ_OK;
+}
+
+extern "C" int oq_int4_linear_host_run(void *plan, oq_stream_t stream) {
+    clear_error();
+    OQ_REQUIRE(plan != nullptr, "null plan");
+    auto *hp = static_cast<HostPlan *>(plan);
+    int dev = 0;
+    OQ_CUDA(cudaGetDevice(&dev));
+    OQ_REQUIRE(dev == hp->device, "the plan was made on device %d, the current device is %d", hp->device, dev);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    OQ_CUDA(cudaGraphLaunch(hp->exec, st));
+    OQ_CUDA(cudaStreamSynchronize(st));
+    return OQ_OK;
+}
+
+extern "C" int oq_int4_linear_host_plan_free(void *plan) {
+    clear_error();
+    if (plan == nullptr) return OQ_OK;
+    auto *hp = static_cast<HostPlan *>(plan);
+    const cudaError_t err = cudaGraphExecDestroy(hp->exec);
+    delete hp;
+    OQ_CUDA(err);
+    return OQ_OK;
+}
+
+extern "C" int oq_int4_linear_host(const void *x, int x_dtype, const uint8_t *packed, const float *scales, void *y,
+                                   int y_dtype, const float *bias, int64_t m, int64_t n, int64_t k, int group_size,
+                                   int kernel, int config, void *x_stage, oq_stream_t stream) {
+    clear_error();
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int rc = host_enqueue(x, x_dtype, packed, scales, y, y_dtype, bias, m, n, k, group_size, kernel, config,
+                                x_stage, st);
     if (rc != OQ_OK) return rc;
     OQ_CUDA(cudaStreamSynchronize(st));
     return OQ_OK;

@@ -17,6 +17,7 @@ from . import tile_table
 __all__ = ["int4_linear", "Int4Linear"]
 
 _YCODES = {torch.float32: nat.OQ_F32, torch.float16: nat.OQ_F16, torch.bfloat16: nat.OQ_BF16}
+_PLANS = 8  # captured host-buffer calls an Int4Linear keeps (forward_host)
 # The current stream's handle of a device without building a Stream object
 # (a decode step calls int4_linear once per layer: host overhead counts).
 _raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
@@ -250,6 +251,7 @@ class Int4Linear:
         self._device = torch.device("cuda", dev)
         self._shapes = {}  # m -> (kernel code, config, from the tuned table)
         self._stages = {}  # (m, k) -> device copy of a host x (forward_host)
+        self._plans = {}  # (x ptr, out ptr, m, k, dtype) -> (plan handle, x, out) (forward_host)
 
     def _choice(self, m, k):
         sel, split = (tile_table.lookup(m, self.out_features, k, self.group_size) if self._kernel is None
@@ -313,12 +315,16 @@ class Int4Linear:
         """The layer on host tensors: x a contiguous (M, K) fp16 / bf16 CPU
         tensor in page-locked memory (``pin_memory()``), the result written
         into `out` -- a page-locked (M, N) CPU tensor of out_dtype, allocated
-        when None -- and returned once it is complete
-        (oq_int4_linear_host: a small kernel copies x over the bus into a
-        device buffer this object keeps per M, while the layer kernel's
-        weights stream; the layer kernel writes y straight into `out`).  The
-        same kernel and result as ``self(x.cuda()).cpu()`` -- bit for bit for
-        decode shapes; the prefill GEMM runs without its stream-K split.  The
+        when None -- and returned once it is complete.  A small kernel copies
+        x over the bus into a device buffer this object keeps per M, while the
+        layer kernel's weights stream; the layer kernel writes y straight into
+        `out`.  The first call with a given (x, out) pair captures both
+        kernels into a CUDA graph (oq_int4_linear_host_plan) that later calls
+        with the same tensors replay -- one graph launch and one
+        synchronization per decode step; the object keeps those tensors alive
+        while it holds their plan (the last _PLANS pairs).  The same kernel
+        and result as ``self(x.cuda()).cpu()`` -- bit for bit for decode
+        shapes; the prefill GEMM runs without its stream-K split.  The
         weights' GPU must be the current device."""
         # (page-locking of x and out is checked by the library, which refuses
         # pageable memory with OQ_ERR_INVALID -> ValueError)
@@ -338,16 +344,45 @@ class Int4Linear:
             out = torch.empty((m, n), dtype=self.out_dtype, pin_memory=True)
         elif out.dtype is not self.out_dtype or out.shape != (m, n) or out.is_cuda or not out.is_contiguous():
             raise ValueError("out must be a contiguous page-locked (M, N) CPU tensor of out_dtype")
+        key = (x.data_ptr(), out.data_ptr(), m, k, code)
+        entry = self._plans.get(key)
+        if entry is None:
+            entry = self._make_plan(x, out, code)
+        st = self._lib.oq_int4_linear_host_run(entry[0], _stream_handle(self._dev))
+        if st:
+            nat.check(st)
+        return out
+
+    def _make_plan(self, x, out, code):
+        import ctypes
+
+        m, k = x.shape
+        g, n = self.group_size, self.out_features
         stage = self._stages.get((m, k))
         if stage is None:
             stage = self._stages[(m, k)] = torch.empty((m, k), dtype=torch.float16, device=self._device)
         sel, cfg, from_table, _ = self._shapes.get((m, k)) or self._choice(m, k)
         p, s, b = self._ptrs
-        stream = _stream_handle(self._dev)
         args = (x.data_ptr(), code, p, s, out.data_ptr(), self._ycode, b, m, n, k, g)
-        st = self._lib.oq_int4_linear_host(*args, sel, cfg, stage.data_ptr(), stream)
+        handle = ctypes.c_void_p()
+        st = self._lib.oq_int4_linear_host_plan(*args, sel, cfg, stage.data_ptr(), ctypes.byref(handle))
         if st == nat.OQ_ERR_INVALID and from_table:
-            st = self._lib.oq_int4_linear_host(*args, 0, cfg & ~15, stage.data_ptr(), stream)
+            st = self._lib.oq_int4_linear_host_plan(*args, 0, cfg & ~15, stage.data_ptr(), ctypes.byref(handle))
         if st:
             nat.check(st)
-        return out
+        if len(self._plans) >= _PLANS:  # drop the oldest plan (dicts keep insertion order)
+            old = self._plans.pop(next(iter(self._plans)))
+            self._lib.oq_int4_linear_host_plan_free(old[0])
+        entry = (handle, x, out)  # the plan reads and writes these tensors' memory
+        self._plans[(x.data_ptr(), out.data_ptr(), m, k, code)] = entry
+        return entry
+
+    def __del__(self):
+        plans = getattr(self, "_plans", None)
+        if plans:
+            try:
+                for handle, _, _ in plans.values():
+                    self._lib.oq_int4_linear_host_plan_free(handle)
+            except Exception:  # interpreter shutdown: the process's graphs go with it
+                pass
+            plans.clear()

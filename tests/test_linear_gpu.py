@@ -543,6 +543,47 @@ def test_int4_linear_forward_host(case):
         layer.forward_host(x)
 
 
+def test_forward_host_plan_replays_new_inputs():
+    """A captured host call (Int4Linear's plan for one (x, out) pair) reads x
+    at every run: new contents of the same page-locked x give the new result;
+    more (x, out) pairs than the plan cache holds still compute correctly;
+    and the uncaptured C entry point oq_int4_linear_host agrees bit for bit."""
+    from openquant.groupwise import quantize_int4_groupwise
+    from openquant.triton_int4 import Int4Linear
+    from openquant_b200.triton_int4 import _PLANS
+    from openquant_b200 import _native as nat
+
+    m, n, k, g = 1, 4096, 4096, 128
+    gen = torch.Generator(device="cuda").manual_seed(11)
+    q = quantize_int4_groupwise(torch.randn(n, k, device="cuda", generator=gen).mul_(0.02), g)
+    layer = Int4Linear(q.data, q.scales, n, g, static_weights=True)
+    x_host = torch.empty(m, k, dtype=torch.float16, pin_memory=True)
+    out = torch.empty(m, n, pin_memory=True)
+    for i in range(3):
+        x = torch.randn(m, k, device="cuda", generator=gen).half()
+        x_host.copy_(x.cpu())
+        assert layer.forward_host(x_host, out=out) is out
+        assert torch.equal(out, layer(x).cpu()), i
+    pairs = [(torch.randn(m, k, generator=torch.Generator().manual_seed(i)).half().pin_memory(),
+              torch.empty(m, n, pin_memory=True)) for i in range(_PLANS + 3)]
+    for xh, yh in pairs + pairs[:2]:
+        assert torch.equal(layer.forward_host(xh, out=yh), layer(xh.cuda()).cpu())
+    assert len(layer._plans) <= _PLANS
+    lib = nat.load()
+    xh, yh = pairs[0]
+    y2 = torch.empty(m, n, pin_memory=True)
+    stage = torch.empty(m, k, dtype=torch.float16, device="cuda")
+    st = lib.oq_int4_linear_host(xh.data_ptr(), nat.OQ_F16, q.data.data_ptr(), q.scales.data_ptr(), y2.data_ptr(),
+                                 nat.OQ_F32, None, m, n, k, g, 0, nat.CONFIG_STATIC_WEIGHTS, stage.data_ptr(),
+                                 nat.stream_of(torch.device("cuda")))
+    assert st == 0, nat.last_error()
+    assert torch.equal(y2, yh)
+    assert lib.oq_int4_linear_host(xh.data_ptr(), nat.OQ_F16, q.data.data_ptr(), q.scales.data_ptr(),
+                                   torch.empty(m, n).data_ptr(), nat.OQ_F32, None, m, n, k, g, 0, 0,
+                                   stage.data_ptr(), nat.stream_of(torch.device("cuda"))) == nat.OQ_ERR_INVALID
+    assert "page-locked" in nat.last_error()
+
+
 @pytest.mark.parametrize("case", [(300, 1000, 2048, 128, torch.bfloat16),   # 16 tiles, each cut over ~9 SMs
                                   (77, 700, 1024, 64, torch.float16),
                                   (300, 19456, 2048, 128, torch.bfloat16),  # 304 tiles: 2 rounds + 8 split
