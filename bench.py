@@ -165,6 +165,10 @@ def summarize(line):
         elif wl.startswith("int4_gemm_llama3"):
             out["prefill_set"] = {c: {"tflops": r3(v["tflops"]), "frac": r3(v["frac"])}
                                   for c, v in a["by_case"].items()}
+            if "gate_up_silu_m2048" in a:
+                sc = a["gate_up_silu_m2048"]
+                out["prefill_gate_up_silu_m2048"] = {"tflops": r3(sc["tflops"]), "frac": r3(sc["frac"]),
+                                                     "speedup_vs_two_gemms": r3(sc["speedup_vs_two_gemms"])}
         elif wl.startswith("int4_gemm_m2048"):
             out["gemm_m2048"] = {"tflops": r3(a["value"]), "frac": r3(a["roofline"]["frac"])}
         elif wl.startswith("int8_gemm"):
@@ -383,7 +387,7 @@ def measure_gemm(dev, peaks, steps=10, warmup=3):
 PREFILL_SHAPES = [("gate_up", 8192, 28672), ("down", 28672, 8192)]
 
 
-def measure_prefill_set(dev, peaks, ms_=(512, 2048, 8192), steps=5, warmup=2):
+def measure_prefill_set(dev, peaks, ms_=(512, 2048, 8192), steps=10, warmup=3):
     """TFLOP/s of the prefill GEMM on the Llama-3-70B MLP shapes (gate/up
     8192->28672, down 28672->8192), bf16 x ~ N(0,1), weights ~ N(0,0.02)
     group 128, at M = 512, 2048 and 8192; two weight copies alternate (each
@@ -451,6 +455,8 @@ def measure_prefill_set(dev, peaks, ms_=(512, 2048, 8192), steps=5, warmup=2):
             del x, y, ws
         del packs, scs, q
         torch.cuda.empty_cache()
+    silu_case = _measure_prefill_silu(dev, peaks, stream, steps, warmup)
+    launches += silu_case.pop("launches")
     return {
         "metric": "INT4 dequant-GEMM TFLOP/s over the Llama-3-70B MLP prefill set",
         "workload": "int4_gemm_llama3_70b_mlp_g128_bf16",
@@ -458,12 +464,82 @@ def measure_prefill_set(dev, peaks, ms_=(512, 2048, 8192), steps=5, warmup=2):
         "unit": "TFLOP/s",
         "value_is": "gate/up at M=2048; every (shape, M) case in by_case",
         "by_case": cases,
+        "gate_up_silu_m2048": silu_case,
         "timing": f"each case after {COOL_DOWN_S} s idle: a kernel timed alone (burst peak), not under the power "
                   "cap the previous case's GEMMs leave behind",
         "gpu_launches": launches,
         "check_rel_l2": rel_worst,
         "check_max_abs": abs_worst,
     }
+
+
+def _measure_prefill_silu(dev, peaks, stream, steps, warmup, m=2048, k=8192, n=28672, g=128):
+    """The Llama-3-70B MLP's gate and up projections fused (silu_gate): the
+    [gate; up] stack of 2 x 28672 rows, K = 8192, M = 2048 bf16 x, one tcgen05
+    GEMM whose epilogue writes silu(gate) * up (28672 features), against the
+    two plain GEMMs it replaces (gate, up: two fp32 outputs, no silu pass).
+    Sampled columns must equal silu(gate) * up of the two GEMMs within a few
+    fp32 ulp."""
+    import ctypes
+
+    import torch
+
+    from openquant_b200 import _native as nat
+    from openquant_b200.groupwise import quantize_int4_groupwise
+
+    lib = nat.load()
+    gen = torch.Generator(device=dev).manual_seed(750)
+    w = torch.randn(2 * n, k, generator=gen, device=dev).mul_(0.02).to(torch.bfloat16)
+    q = quantize_int4_groupwise(w, g)
+    del w
+    x = torch.randn(m, k, generator=gen, device=dev).to(torch.bfloat16)
+    half = q.data.numel() // 2
+    y = torch.empty(m, n, device=dev)
+    yg, yu = torch.empty(m, n, device=dev), torch.empty(m, n, device=dev)
+    tc = nat.KERNELS["tcgen05"]
+
+    def call(packed, scales, out, cols, cfg, h):
+        st = lib.oq_int4_linear(ctypes.c_void_p(x.data_ptr()), nat.OQ_BF16, ctypes.c_void_p(packed.data_ptr()),
+                                ctypes.c_void_p(scales.data_ptr()), ctypes.c_void_p(out.data_ptr()), m, cols, k, g,
+                                tc, cfg, h)
+        if st != 0:
+            raise RuntimeError(nat.last_error())
+
+    def fused(count, h):
+        for _ in range(count):
+            call(q.data, q.scales, y, n, nat.CONFIG_SILU_GATE, h)
+
+    def separate(count, h):
+        for _ in range(count):
+            call(q.data[:half], q.scales[:n], yg, n, 0, h)
+            call(q.data[half:], q.scales[n:], yu, n, 0, h)
+
+    torch.cuda.synchronize()
+    out = {"launches": 0}
+    for name, body in (("fused", fused), ("two_gemms", separate)):
+        with torch.cuda.stream(stream):
+            body(warmup, ctypes.c_void_p(stream.cuda_stream))
+        stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            body(steps, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        graph.replay()
+        torch.cuda.synchronize()
+        time.sleep(COOL_DOWN_S)
+        out[name + "_ms"] = _device_timed(stream, graph.replay, steps)
+        del graph
+        out["launches"] += (warmup + 2 * steps) * (1 if name == "fused" else 2)
+    cols = torch.arange(0, n, 997, device=dev)
+    gsel, usel = yg[:, cols].double(), yu[:, cols].double()
+    ref = gsel * torch.sigmoid(gsel) * usel
+    err = (y[:, cols].double() - ref).abs()
+    assert float((err - 2e-6 * ref.abs()).max()) <= 1e-6, float(err.max())
+    flops = 2.0 * m * (2 * n) * k
+    out["tflops"] = flops / (out["fused_ms"] / 1e3) / 1e12
+    out["frac"] = out["tflops"] / peaks["bf16_tflops"]
+    out["speedup_vs_two_gemms"] = out["two_gemms_ms"] / out["fused_ms"]
+    out["check"] = "sampled columns equal silu(gate) * up of the two plain GEMMs within 2e-6 relative + 1e-6"
+    return out
 
 
 DECODE_LAYERS = [("qkv", 4096, 12288), ("o_proj", 4096, 4096), ("gate_up", 4096, 22016), ("down", 11008, 4096)]

@@ -89,8 +89,11 @@ typedef void *oq_stream_t; /* a cudaStream_t */
 /* oq_int4_linear / oq_int4_linear_ex `config` flag: SiLU-gate fusion of a
  * gate/up pair.  packed and scales hold the [gate; up] stack -- 2n rows,
  * gate rows first -- and y (M x n) = silu(x . Wg^T) * (x . Wu^T) with
- * silu(g) = g / (1 + exp(-g)), in one GEMV pass (M <= 16, no bias).  No
- * counterpart in the reference. */
+ * silu(g) = g / (1 + exp(-g)), in one pass, no bias: the GEMV for M <= 16
+ * (kernel AUTO or GEMV), else (or kernel TCGEN05) the tcgen05 GEMM, whose
+ * 128-row tiles hold the gate and up rows of 64 features and whose epilogue
+ * writes silu(gate) * up (never split over a workspace).  No counterpart in
+ * the reference. */
 #define OQ_CONFIG_SILU_GATE 64
 
 /* Library version string ("openquant_b200 <x.y.z> sm_100a"). */

@@ -162,11 +162,70 @@ __global__ void __launch_bounds__(256) streamk_fixup_kernel(const float *__restr
     }
 }
 
+// SiLU-gate tiles (gate_n > 0): the weights are an MLP's [gate; up] stack
+// of n = 2 gate_n rows and the output y = silu(x . Wg^T) * (x . Wu^T) has
+// gate_n features.  A 128-row tile then holds 64 features: in TMEM lane
+// quarter q, lanes 0-15 are the gate rows of features f0 + 16 q + (0..15) and
+// lanes 16-31 the up rows of the same features, so the epilogue pairs them
+// with one shuffle.  f0 = 64 (tile / tiles_m) = n0 / 2.  Gate rows past gate_n
+// read up rows and up rows past n read zeros (TMA fill); neither is stored.
+__device__ __forceinline__ int tile_weight_row(int gate_n, int n0, int r) {
+    if (gate_n == 0) return n0 + r;
+    const int q = r >> 5, l = r & 31;
+    return ((l & 16) ? gate_n : 0) + (n0 >> 1) + 16 * q + (l & 15);
+}
+
+// The packed tile of one k-block: one 128-row TMA box, or in SiLU-gate mode
+// eight 16-row boxes (smem rows 16 b ..: gate rows for even b, up rows for
+// odd b, of lane quarter b / 2) -- the same 4 KB either way.
+__device__ __forceinline__ void load_weight_tile(uint8_t *dst, const CUtensorMap *wmap, uint64_t *bar, int kb,
+                                                 int n0, int gate_n) {
+    if (gate_n == 0) {
+        tma_load_2d(dst, wmap, bar, kb * (kBK / 2), n0);
+        return;
+    }
+#pragma unroll
+    for (int b = 0; b < 8; ++b)
+        tma_load_2d(dst + b * 16 * (kBK / 2), wmap, bar, kb * (kBK / 2),
+                    ((b & 1) ? gate_n : 0) + (n0 >> 1) + 16 * (b >> 1));
+}
+
+// Epilogue of a run of 32 batch rows of one TMEM lane: y.store_run, or in
+// SiLU-gate mode silu(gate) * up.  There lane l < 16 holds the gate sums of
+// feature l and lane l + 16 the up sums: the partners swap their values, lane
+// l computes batch rows 0-15 of feature l and lane l + 16 rows 16-31, so all
+// 32 lanes share the work.  silu(g) = g / (1 + e^-g) with the fast exp and
+// division intrinsics (a few ulp): the epilogue holds the tile's TMEM
+// accumulator until it is done, so its cost is on the GEMM's critical path.
+template <int CNT>
+__device__ __forceinline__ void store_tile_run(const OutSpec &y, int64_t b0, int64_t bend, int n, int gate_n, int n0,
+                                               int q, int lane, uint32_t (&v)[CNT]) {
+    static_assert(CNT == 32, "one TMEM load of 32 batch rows");
+    if (gate_n == 0) {
+        const int row = n0 + q * 32 + lane;
+        if (row < n) y.store_run(b0, bend, row, v);
+        return;
+    }
+    const bool lo = lane < 16;
+    uint32_t o[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+        // partner values of rows j and j + 16 (xor 16: gate <-> up lane)
+        const float pa = __shfl_xor_sync(0xffffffffu, __uint_as_float(v[j]), 16);
+        const float pb = __shfl_xor_sync(0xffffffffu, __uint_as_float(v[j + 16]), 16);
+        const float g = lo ? __uint_as_float(v[j]) : pb;
+        const float u = lo ? pa : __uint_as_float(v[j + 16]);
+        o[j] = __float_as_uint(__fdividef(g, 1.0f + __expf(-g)) * u);
+    }
+    const int f = (n0 >> 1) + 16 * q + (lane & 15);
+    if (f < gate_n) y.store_run(b0 + (lo ? 0 : 16), bend, f, o);
+}
+
 template <typename XT>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_int4_tcgen05_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
                              const float *__restrict__ scales, OutSpec y, int m, int n, int kp, int g, int t0,
-                             float *__restrict__ ws) {
+                             float *__restrict__ ws, int gate_n) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
     uint8_t *xbuf = smem;                                    // [S][256 rows][128 B], swizzled
@@ -224,7 +283,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (r > 0 && !(ok = mbar_wait(&empty[s], (r - 1) & 1))) break;
                     mbar_arrive_expect_tx(&full[s], kXBytes + kWBytes);
                     tma_load_2d(xbuf + (size_t)s * kXBytes, &xmap, &full[s], kb * kBK, m0);
-                    tma_load_2d(wbuf + (size_t)s * kWBytes, &wmap, &full[s], kb * (kBK / 2), n0);
+                    load_weight_tile(wbuf + (size_t)s * kWBytes, &wmap, &full[s], kb, n0, gate_n);
                 }
             }
             // Drain: every issued stage's copies must land before the CTA
@@ -274,7 +333,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         int tile, kb0, kb1, pi;
         while (ok && seg.next(tile, kb0, kb1, pi)) {
             const int n0 = (tile / tiles_m) * kBN;
-            const float *srow = scales + (size_t)min(n0 + r, n - 1) * groups;
+            const float *srow = scales + (size_t)min(tile_weight_row(gate_n, n0, r), n - 1) * groups;
             for (int kb = kb0; kb < kb1; ++kb, ++it) {
                 const int s = it % kStages, rd = it / kStages;
                 const int c0 = kb * kBK;
@@ -338,8 +397,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = __all_sync(0xffffffffu, mbar_wait(acc_full, ti & 1));  // tcgen05.ld is .sync.aligned
             if (!ok) break;
             tc_fence_after();
-            const int row = n0 + q * 32 + lane;
-            const bool piece = kb0 != 0 || kb1 != kblocks;
+            const bool piece = kb0 != 0 || kb1 != kblocks;  // (never in SiLU-gate mode)
             float *slot = ws + (2 * (size_t)blockIdx.x + (pi == 0 ? 0 : 1)) * (size_t)(kAccCols * kBN);
 #pragma unroll 1
             for (int c = 0; c < kAccCols / 32; ++c) {
@@ -348,8 +406,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_wait_ld();
                 if (piece)
                     store_piece(slot, c, q * 32 + lane, v);
-                else if (row < n)
-                    y.store_run(m0 + c * 32, m, row, v);
+                else
+                    store_tile_run(y, m0 + c * 32, m, n, gate_n, n0, q, lane, v);
             }
             tc_fence_before();
             __syncwarp();
@@ -391,7 +449,7 @@ template <typename XT>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_int4_tcgen05_wide_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
                                   const float *__restrict__ scales, OutSpec y, int m, int n, int kp, int g, int nb,
-                                  int t0, float *__restrict__ ws) {
+                                  int t0, float *__restrict__ ws, int gate_n) {
     static_assert(kDqSplit == 1, "the wide kernel keeps one dequant warp per TMEM lane quarter");
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
@@ -458,7 +516,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     mbar_arrive_expect_tx(&full[s], tx);
                     tma_load_2d(xs, &xmap, &full[s], kb * kBK, m0);
                     tma_load_2d(xs + nb * 128, &xmap, &full[s], kb * kBK, m0 + nb);
-                    tma_load_2d(wbuf + (size_t)s * kWBytes, &wmap, &full[s], kb * (kBK / 2), n0);
+                    load_weight_tile(wbuf + (size_t)s * kWBytes, &wmap, &full[s], kb, n0, gate_n);
                 }
             }
             // Drain: every issued stage's copies land before the CTA exits.
@@ -509,7 +567,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         int tile, kb0, kb1, pi;
         while (ok && seg.next(tile, kb0, kb1, pi)) {
             const int n0 = (tile / tiles_m) * kBN;
-            const float *srow = scales + (size_t)min(n0 + r, n - 1) * groups;
+            const float *srow = scales + (size_t)min(tile_weight_row(gate_n, n0, r), n - 1) * groups;
             for (int kb = kb0; kb < kb1; ++kb, ++it) {
                 const int s = it % kWideStages, a = it & 1;
                 const int c0 = kb * kBK;
@@ -560,8 +618,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = __all_sync(0xffffffffu, mbar_wait(acc_full, ti & 1));  // tcgen05.ld is .sync.aligned
             if (!ok) break;
             tc_fence_after();
-            const int row = n0 + q * 32 + lane;
-            const bool piece = kb0 != 0 || kb1 != kblocks;
+            const bool piece = kb0 != 0 || kb1 != kblocks;  // (never in SiLU-gate mode)
             float *slot = ws + (2 * (size_t)blockIdx.x + (pi == 0 ? 0 : 1)) * (size_t)(bx * kBN);
 #pragma unroll 1
             for (int c = 0; c < bx / 32; ++c) {
@@ -570,8 +627,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_wait_ld();
                 if (piece)
                     store_piece(slot, c, q * 32 + lane, v);
-                else if (row < n)
-                    y.store_run(m0 + c * 32, m, row, v);
+                else
+                    store_tile_run(y, m0 + c * 32, m, n, gate_n, n0, q, lane, v);
             }
             tc_fence_before();
             __syncwarp();
@@ -669,10 +726,11 @@ inline GemmPlan plan_gemm(int64_t m, int64_t n, int64_t k, int g, bool allow_spl
     return best;
 }
 
+// n: weight rows (2 gate_n in SiLU-gate mode, which never splits).
 template <typename XT>
 int launch(const XT *x, CUtensorMapDataType xtype, const uint8_t *packed, const float *scales, OutSpec y, int64_t m,
-           int64_t n, int64_t k, int g, void *ws, size_t ws_bytes, cudaStream_t st) {
-    GemmPlan plan = plan_gemm(m, n, k, g, ws != nullptr);
+           int64_t n, int64_t k, int g, void *ws, size_t ws_bytes, int64_t gate_n, cudaStream_t st) {
+    GemmPlan plan = plan_gemm(m, n, k, g, ws != nullptr && gate_n == 0);
     if (plan.split && ws_bytes < plan.ws_bytes) plan = plan_gemm(m, n, k, g, false);
     const int64_t kp = cdiv(k, g) * g;
     CUtensorMap xmap, wmap;
@@ -680,7 +738,7 @@ int launch(const XT *x, CUtensorMapDataType xtype, const uint8_t *packed, const 
                                 (uint32_t)(plan.wide ? plan.nb : kBX), CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc != OQ_OK) return rc;
     rc = make_tensor_map_2d(&wmap, packed, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)(kp / 2), (uint64_t)n,
-                            (uint64_t)(kp / 2), kBK / 2, kBN, CU_TENSOR_MAP_SWIZZLE_NONE);
+                            (uint64_t)(kp / 2), kBK / 2, gate_n ? 16 : kBN, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc != OQ_OK) return rc;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)plan.grid);
@@ -699,13 +757,14 @@ int launch(const XT *x, CUtensorMapDataType xtype, const uint8_t *packed, const 
         if (rc != OQ_OK) return rc;
         cfg.dynamicSmemBytes = kWideSmemBytes;
         err = cudaLaunchKernelEx(&cfg, kern, xmap, wmap, scales, y, (int)m, (int)n, (int)kp, g, plan.nb, (int)plan.t0,
-                                 wsf);
+                                 wsf, (int)gate_n);
     } else {
         auto kern = gemm_int4_tcgen05_kernel<XT>;
         rc = allow_smem(reinterpret_cast<const void *>(kern), kSmemBytes);
         if (rc != OQ_OK) return rc;
         cfg.dynamicSmemBytes = kSmemBytes;
-        err = cudaLaunchKernelEx(&cfg, kern, xmap, wmap, scales, y, (int)m, (int)n, (int)kp, g, (int)plan.t0, wsf);
+        err = cudaLaunchKernelEx(&cfg, kern, xmap, wmap, scales, y, (int)m, (int)n, (int)kp, g, (int)plan.t0, wsf,
+                                 (int)gate_n);
     }
     if (err != cudaSuccess) {
         set_error("int4_linear (tcgen05 GEMM): launch failed: %s", cudaGetErrorString(err));
@@ -758,12 +817,14 @@ int gemm_tcgen05_supported(int64_t m, int64_t n, int64_t k, int g, const void *x
 }
 
 int gemm_tcgen05_launch(const void *x, int x_dtype, const uint8_t *packed, const float *scales, OutSpec y, int64_t m,
-                        int64_t n, int64_t k, int g, void *ws, size_t ws_bytes, cudaStream_t st) {
+                        int64_t n, int64_t k, int g, void *ws, size_t ws_bytes, cudaStream_t st, int64_t gate_n) {
+    // gate_n > 0: SiLU-gate mode -- `packed` / `scales` hold the [gate; up]
+    // stack of n = 2 gate_n rows and y gets gate_n features (no workspace).
     if (x_dtype == OQ_BF16)
         return launch(static_cast<const __nv_bfloat16 *>(x), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, packed, scales, y, m,
-                      n, k, g, ws, ws_bytes, st);
+                      n, k, g, ws, ws_bytes, gate_n, st);
     return launch(static_cast<const __half *>(x), CU_TENSOR_MAP_DATA_TYPE_FLOAT16, packed, scales, y, m, n, k, g, ws,
-                  ws_bytes, st);
+                  ws_bytes, gate_n, st);
 }
 
 size_t gemm_tcgen05_workspace_bytes(int64_t m, int64_t n, int64_t k, int g) {

@@ -17,7 +17,8 @@ namespace oq {
 int gemm_tcgen05_supported(int64_t m, int64_t n, int64_t k, int g, const void *x, const uint8_t *packed,
                            const float *y);
 int gemm_tcgen05_launch(const void *x, int x_dtype, const uint8_t *packed, const float *scales, OutSpec y,
-                        int64_t m, int64_t n, int64_t k, int g, void *ws, size_t ws_bytes, cudaStream_t st);
+                        int64_t m, int64_t n, int64_t k, int g, void *ws, size_t ws_bytes, cudaStream_t st,
+                        int64_t gate_n = 0);
 size_t gemm_tcgen05_workspace_bytes(int64_t m, int64_t n, int64_t k, int g);
 
 namespace {
@@ -1616,10 +1617,19 @@ int int4_linear_impl(const void *x, int x_dtype, const uint8_t *packed, const fl
     const int64_t kp = cdiv(k, group_size) * group_size;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (config & OQ_CONFIG_SILU_GATE) {
-        OQ_REQUIRE(kernel == OQ_KERNEL_AUTO || kernel == OQ_KERNEL_GEMV, "SiLU-gate fusion runs on the GEMV kernel");
+        OQ_REQUIRE(kernel == OQ_KERNEL_AUTO || kernel == OQ_KERNEL_GEMV || kernel == OQ_KERNEL_TCGEN05,
+                   "SiLU-gate fusion runs on the GEMV (M <= 16) or the tcgen05 GEMM");
         OQ_REQUIRE(y.bias == nullptr, "SiLU-gate fusion takes no bias");
+        OQ_REQUIRE(n < (1ll << 30), "SiLU-gate fusion: too many features");
+        const bool on_gemv = kernel == OQ_KERNEL_GEMV || (kernel == OQ_KERNEL_AUTO && m <= 16 &&
+                                                          gemv_supported(m, 2 * n, k, group_size, x, packed));
+        if (!on_gemv) {
+            OQ_REQUIRE(gemm_tcgen05_supported(m, 2 * n, k, group_size, x, packed, nullptr),
+                       "SiLU-gate fusion: the tcgen05 GEMM does not take this shape/alignment");
+            return gemm_tcgen05_launch(x, x_dtype, packed, scales, y, m, 2 * n, k, group_size, nullptr, 0, st, n);
+        }
         OQ_REQUIRE(m <= 16 && gemv_supported(m, 2 * n, k, group_size, x, packed),
-                   "SiLU-gate fusion needs M <= 16 and a shape the GEMV takes");
+                   "SiLU-gate fusion on the GEMV needs M <= 16 and a shape the GEMV takes");
         if (x_dtype == OQ_F16)
             return launch_gemv_gate(static_cast<const __half *>(x), packed, scales, y, m, n, k, kp, group_size, config, st);
         return launch_gemv_gate(static_cast<const __nv_bfloat16 *>(x), packed, scales, y, m, n, k, kp, group_size,

@@ -62,7 +62,9 @@ def int4_linear(x, packed, scales, out_features, group_size, *, block_m=64, bloc
     silu_gate=True fuses the gate/up pair of an MLP: `packed` and `scales`
     hold the [gate; up] stack (2 * out_features rows, gate first) and y is
     silu(x . Wg^T) * (x . Wu^T) with silu(g) = g / (1 + exp(-g)), computed in
-    one GEMV pass (M <= 16, no bias).
+    one pass (no bias): the decode GEMV for M <= 16, else the tcgen05 GEMM,
+    whose tiles pair each feature's gate and up rows so its epilogue writes
+    silu(gate) * up directly.
 
     static_weights=True declares that `packed` and `scales` were written
     before any kernel still in flight on the stream (quantized at load time
@@ -100,8 +102,8 @@ def int4_linear(x, packed, scales, out_features, group_size, *, block_m=64, bloc
         raise ValueError("Incorrect scales shape")
     if packed.numel() != rows * kp // 2:
         raise ValueError("Incorrect packed weight count")
-    if silu_gate and (bias is not None or m > 16):
-        raise ValueError("silu_gate takes no bias and needs M <= 16")
+    if silu_gate and bias is not None:
+        raise ValueError("silu_gate takes no bias")
     if not packed.is_contiguous() or not scales.is_contiguous():
         raise ValueError("Weights and scales must be contiguous")
     dev = x.get_device()
@@ -145,9 +147,9 @@ def int4_linear(x, packed, scales, out_features, group_size, *, block_m=64, bloc
                 launch_f16s()
         return out
     if silu_gate:
-        if kernel not in (None, "gemv"):
-            raise ValueError("silu_gate runs on the GEMV kernel")
-        sel, split = nat.KERNELS["gemv"], nat.CONFIG_SILU_GATE
+        if kernel not in (None, "gemv", "tcgen05"):
+            raise ValueError("silu_gate runs on the GEMV (M <= 16) or the tcgen05 GEMM")
+        sel, split = nat.KERNELS[kernel or "auto"], nat.CONFIG_SILU_GATE
     elif kernel is None:
         sel, split = tile_table.lookup(m, n, k, g)
     else:

@@ -543,6 +543,70 @@ def test_int4_linear_forward_host(case):
         layer.forward_host(x)
 
 
+@pytest.mark.parametrize("shape", [(77, 300, 512, 32, torch.float16), (300, 1000, 2048, 128, torch.bfloat16),
+                                   (2048, 700, 1024, 128, torch.bfloat16), (17, 2000, 4096, 128, torch.float16),
+                                   (40, 64, 256, 64, torch.float16), (8, 100, 1024, 128, torch.bfloat16)])
+def test_silu_gate_fusion_prefill_gemm(shape):
+    """silu_gate on the tcgen05 GEMM (M > 16, or kernel="tcgen05"): tiles
+    pair each feature's gate and up rows and the epilogue writes
+    silu(gate) * up.  Equal to silu(gate) * up of two plain GEMM launches
+    (the same sums; silu from expf vs torch's sigmoid in fp64: a few ulp),
+    within the parity bar of the oracle's two products, through int4_linear,
+    with bf16 output, and unchanged when a workspace is offered (the fused
+    GEMM never splits)."""
+    from openquant.groupwise import quantize_int4_groupwise
+    from openquant.triton_int4 import int4_linear
+    from openquant_b200 import _native as nat
+
+    m, n, k, g, dtype = shape
+    gen = torch.Generator(device="cuda").manual_seed(3 * n + k)
+    w = torch.randn(2 * n, k, device="cuda", generator=gen).mul_(0.02).to(dtype)
+    q = quantize_int4_groupwise(w, g)
+    x = torch.randn(m, k, device="cuda", generator=gen).to(dtype)
+    code = nat.OQ_F16 if dtype == torch.float16 else nat.OQ_BF16
+    lib = nat.load()
+    half = q.data.numel() // 2
+    tc = nat.KERNELS["tcgen05"]
+
+    def run(packed, scales, out_cols, kernel, cfg):
+        y = torch.empty(m, out_cols, device="cuda")
+        nat.check(lib.oq_int4_linear(nat.ptr(x), code, nat.ptr(packed), nat.ptr(scales), nat.ptr(y), m, out_cols, k,
+                                     g, kernel, cfg, nat.stream_of(x.device)))
+        return y
+
+    gate = run(q.data[:half], q.scales[:n], n, tc, 0)
+    up = run(q.data[half:], q.scales[n:], n, tc, 0)
+    fused = run(q.data, q.scales, n, tc, nat.CONFIG_SILU_GATE)
+    assert_no_device_error()
+    ref = (gate.double() * torch.sigmoid(gate.double())) * up.double()
+    err = (fused.double() - ref).abs()
+    assert float((err - 2e-6 * ref.abs()).max()) <= 1e-6, float(err.max())
+    if m > 16:
+        assert torch.equal(run(q.data, q.scales, n, 0, nat.CONFIG_SILU_GATE), fused)
+        assert torch.equal(int4_linear(x, q.data, q.scales, n, g, silu_gate=True), fused)
+    assert torch.equal(int4_linear(x, q.data, q.scales, n, g, silu_gate=True, kernel="tcgen05"), fused)
+    ws = torch.empty(64 << 20, dtype=torch.uint8, device="cuda")
+    y_ws = torch.empty(m, n, device="cuda")
+    nat.check(lib.oq_int4_linear_ws(nat.ptr(x), code, nat.ptr(q.data), nat.ptr(q.scales), nat.ptr(y_ws), nat.OQ_F32,
+                                    None, m, n, k, g, tc, nat.CONFIG_SILU_GATE, nat.ptr(ws), ws.numel(),
+                                    nat.stream_of(x.device)))
+    assert torch.equal(y_ws, fused)
+    name = "f16" if dtype == torch.float16 else "bf16"
+    data, scales = q.data.cpu().numpy(), q.scales.cpu().numpy()
+    xf = x.float().cpu().numpy()
+    g_ref = orc.int4_linear(xf, data[:half], scales[:n], n, g, x_dtype=name)
+    u_ref = orc.int4_linear(xf, data[half:], scales[n:], n, g, x_dtype=name)
+    silu = g_ref / (1.0 + np.exp(-g_ref))
+    ref_o = silu * u_ref
+    err_o = fused.double().cpu().numpy() - ref_o
+    assert (np.abs(err_o) <= MAX_ABS * (1.1 * np.abs(u_ref) + np.abs(silu)) + 1e-6).all()
+    assert np.linalg.norm(err_o) / np.linalg.norm(ref_o) <= 2 * REL_L2
+    yb = int4_linear(x, q.data, q.scales, n, g, silu_gate=True, kernel="tcgen05", out_dtype=torch.bfloat16)
+    assert torch.equal(yb, fused.to(torch.bfloat16))
+    with pytest.raises(ValueError):
+        int4_linear(x, q.data, q.scales, n, g, silu_gate=True, kernel="simt")
+
+
 def test_forward_host_plan_replays_new_inputs():
     """A captured host call (Int4Linear's plan for one (x, out) pair) reads x
     at every run: new contents of the same page-locked x give the new result;
