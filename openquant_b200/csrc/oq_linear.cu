@@ -212,17 +212,18 @@ __device__ __forceinline__ void gemv_stage_x(const XT *__restrict__ x, XT *xs, f
 // (same layout, same bias table entries, same summation order), so the warp
 // can start on its chunks after a __syncwarp instead of a barrier over the
 // whole CTA: the other warps' x loads no longer gate it.  Lane l stages
-// vectors l and l + 32 of the warp's 64 per row (chunk q = vector / 16), two
-// rows per pass, all four loads issued first.  Warps of the two tile groups
-// with the same wg write the same values.
-template <typename XT, bool SA, bool FOLD>
+// vectors l and l + 32 of the warp's 64 per row (chunk q = vector / 16), RP
+// rows per pass with all their loads issued first (one L2 round trip per RP
+// rows).  Warps of the two tile groups with the same wg write the same
+// values.
+template <typename XT, bool SA, bool FOLD, int RP>
 __device__ __forceinline__ void gemv_stage_x_warp(const XT *__restrict__ x, XT *xs, float *corr, int m, int k,
                                                   int xstride, int wg, int lane, int nchunks) {
     const int kv = k / 8;
-    for (int r0 = 0; r0 < m; r0 += 2) {
-        uint4 v[2][2];
+    for (int r0 = 0; r0 < m; r0 += RP) {
+        uint4 v[RP][2];
 #pragma unroll
-        for (int rr = 0; rr < 2; ++rr)
+        for (int rr = 0; rr < RP; ++rr)
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 const int r = r0 + rr, i = lane + 32 * h, c = wg + 8 * (i >> 4), cv = 16 * c + (i & 15);
@@ -231,11 +232,12 @@ __device__ __forceinline__ void gemv_stage_x_warp(const XT *__restrict__ x, XT *
                                : make_uint4(0, 0, 0, 0);
             }
 #pragma unroll
-        for (int rr = 0; rr < 2; ++rr)
+        for (int rr = 0; rr < RP; ++rr) {
+            if (r0 + rr >= m) break;  // warp-uniform
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 const int r = r0 + rr, i = lane + 32 * h, c = wg + 8 * (i >> 4), cv = 16 * c + (i & 15);
-                const bool live = r < m && c < nchunks;
+                const bool live = c < nchunks;
                 const uint4 w = SA ? sa_perm_x(v[rr][h]) : v[rr][h];
                 if (live) reinterpret_cast<uint4 *>(xs)[r * (xstride / 8) + cv] = w;
                 if (FOLD) {  // warp-uniform: every lane takes part in the shuffles
@@ -249,6 +251,7 @@ __device__ __forceinline__ void gemv_stage_x_warp(const XT *__restrict__ x, XT *
                     if (live && (i & 15) == 0) corr[c * 16 + r] = t;
                 }
             }
+        }
     }
 }
 
@@ -958,7 +961,7 @@ __global__ void __launch_bounds__(512, 2)
     if (grp >= ntiles) return;  // no second tile: the second warp group is done
     asm volatile("griddepcontrol.wait;" ::: "memory");
     // Each warp stages the x its own chunks read: no CTA-wide barrier after the wait.
-    if (XS) gemv_stage_x_warp<XT, SA, FOLD>(x, xs, corr, m, k, xstride, wg, lane, nchunks);
+    if (XS) gemv_stage_x_warp<XT, SA, FOLD, 2 * NT>(x, xs, corr, m, k, xstride, wg, lane, nchunks);
     __syncwarp();
 
     const uint8_t *wst = smem + grp * stage_pitch;
