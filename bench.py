@@ -143,10 +143,10 @@ def headline_config(world):
         "m": M, "k": K, "n": N, "group_size": G,
         "weights": f"{COPIES} distinct INT4 copies rotated ({COPIES * ALG_BYTES / 1e6:.0f} MB > L2)",
         "l2": "inputs larger than L2 (weight-copy rotation), no flush",
-        "launch": "CUDA graphs of back-to-back launches (programmatic dependent launch): up to 8 of the W "
-                  "warm-up launches eagerly, then behind a device-side sleep (so the host's submission is off the "
-                  "clock) the other warm-up launches, the start event, the K timed launches (one graph up to "
-                  f"{ONE_GRAPH_MAX} launches), the end event",
+        "launch": "CUDA graphs of back-to-back launches (programmatic dependent launch): the first of the W "
+                  "warm-up launches eagerly (kernel set-up), then behind a device-side sleep (so the host's "
+                  "submission is off the clock) the other W-1 warm-up launches, the start event, the K timed "
+                  f"launches (one graph up to {ONE_GRAPH_MAX} launches), the end event",
         "static_weights": "weights quantized at setup and synchronized, so each launch streams them "
                           "while the previous one drains (OQ_CONFIG_STATIC_WEIGHTS); x and y stay ordered",
         "parallelism": f"dp{world} (each rank streams its own weight copies)",
@@ -1363,22 +1363,26 @@ def run_ours(args):
         upload_graph(g, stream)
         return g
 
-    # Warm-up, exactly W launches: the first (up to 8) eagerly -- the kernels'
-    # first-launch set-up happens there, before any capture -- the rest as a
-    # graph replayed right before the timed launches.
-    eager = min(args.warmup, 8)
+    # Warm-up, exactly W launches: the first eagerly and synchronized -- the
+    # kernel's first-launch set-up happens there, before any capture -- the
+    # rest right before the timed launches, behind the device-side sleep
+    # (up to 64 as plain launches, more as a graph), so that the timed
+    # launches follow warm-up launches on the GPU.
+    eager = min(args.warmup, 1)
     with torch.cuda.stream(stream):
         launch_many(eager, ctypes.c_void_p(stream.cuda_stream))
     stream.synchronize()
     chunk = 1024
     rest_w = args.warmup - eager
     if rest_w + args.steps <= ONE_GRAPH_MAX:
-        graphs = {"warm": make_graph(eager, rest_w) if rest_w else None,
+        graphs = {"warm": make_graph(eager, rest_w) if rest_w > 64 else None,
                   "timed": make_graph(args.warmup, args.steps)}
 
         def warm():
             if graphs["warm"] is not None:
                 graphs["warm"].replay()
+            elif rest_w:
+                launch_many(rest_w, ctypes.c_void_p(stream.cuda_stream), first=eager)
 
         def timed():
             graphs["timed"].replay()
