@@ -591,7 +591,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW <= 8 ? 2 : 1)
                 const int ti = pos / spt, st = pos - ti * spt;
                 const int row0 = tile_row0(ti);
                 const int k0 = st * L::kStageCols;
-                mbar_arrive_expect_tx(&full[slot], L::kStageBytes + (STMA ? 16 * spr * 4 : 0));
+                mbar_arrive_expect_tx(&full[slot], L::kStageBytes + (STMA ? 16 * spr * (half_scales ? 2 : 4) : 0));
 #pragma unroll
                 for (int b = 0; b < L::kBoxes; ++b)
                     tma_load_2d(wbuf + (size_t)slot * L::kStageBytes + b * 2048, &wmap, &full[slot], k0 / 2 + 128 * b,
@@ -680,10 +680,15 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW <= 8 ? 2 : 1)
                 }
                 const int scol = (cs * 128 + 32 * t) >> gshift;
                 float sa, sb;
-                if (STMA)
+                if (STMA && half_scales) {  // fp16 scale box: 16 rows of spr halves, unswizzled
+                    const __half *sh = reinterpret_cast<const __half *>(sst);
+                    sa = __half2float(sh[gi * spr + scol]);
+                    sb = __half2float(sh[(gi + 8) * spr + scol]);
+                } else if (STMA) {
                     stage_scales(sst, gi, scol, spr, sa, sb);
-                else
+                } else {
                     sa = sreg[q][0], sb = sreg[q][1];
+                }
                 const bool in = 128 * c + 32 * t < kp;
                 if constexpr (SA) {
                     gemv_chunk_sa<NT, XS, FOLD, true>(c, qa, qb, in ? sa : 0.0f, in ? sb : 0.0f, xaddr, xon, xg, xb, acc,
@@ -1262,9 +1267,19 @@ int launch_gemv_tma(const XT *x, const uint8_t *packed, const float *scales, Out
     if (stages == 0) return invalid("TMA GEMV: shape does not fit in shared memory");
     CUtensorMap wmap, smap;
     bool stma = false;
-    const int rc = make_gemv_maps<CW, CPW>(packed, scales, n, kp, g, &wmap, &smap, &stma);
+    int rc = make_gemv_maps<CW, CPW>(packed, scales, n, kp, g, &wmap, &smap, &stma);
     if (rc != OQ_OK) return rc;
-    if (half_scales) stma = false;  // fp16 scales: each lane loads its own
+    if (half_scales) {
+        // fp16 scales by TMA too: a box of the stage's groups x 16 rows
+        // (2-byte elements, rows of groups * 2 bytes), read unswizzled
+        const int64_t groups = kp / g, spr = L::kStageCols / g;
+        stma = (groups * 2) % 16 == 0 && (spr * 2) % 16 == 0 && aligned(scales, 16);
+        if (stma) {
+            rc = make_tensor_map_2d(&smap, scales, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)groups, (uint64_t)n,
+                                    (uint64_t)(groups * 2), (uint32_t)spr, 16, CU_TENSOR_MAP_SWIZZLE_NONE);
+            if (rc != OQ_OK) return rc;
+        }
+    }
     auto pick = [&](auto kern) -> int {
         int rc2 = allow_max_smem(reinterpret_cast<const void *>(kern));
         if (rc2 != OQ_OK) return rc2;
